@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""Benchmark of the HSPMN v2.1 contextual-stream inference path on B200.
+
+Default workload (one JSON line on rank 0): HSPMNBlock eval forward, bf16,
+dim=2048, num_heads=16, num_kv_heads=4 (the config default), k=0.2, S=4096,
+64 sequences per GPU, x ~ N(0,1), default-init weights (seed 42). A step is
+one block forward over the GPU's batch; the router top-K, gather, SQDK
+attention and scatter inside it are this library's sm_100a kernels, the
+projections / norms / RoPE / reflexive stream are stock PyTorch (as in the
+reference). Multi-GPU: one process per GPU (torchrun), every rank runs its
+own 64 sequences with replicated weights and no data-path collective (weak
+scaling); the timed region is bracketed by barriers and the max over ranks is
+reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload block|sqdk-sweep]
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+numpy oracle port of HSPMNBlock.forward) on the host cores, one sequence of
+the same workload per step; under torchrun only rank 0 runs it.
+``--workload sqdk-sweep`` runs the standalone router / gather / SQDK / scatter
+sweep (B=8, S=32768, H=Hkv=16, hd=128, k in {0.05, 0.1, 0.2, 0.5}) and
+prints one line per k.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(REPO, "hspmn-v2.1_b200"), REPO):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "SQDK block tok/s at B=64,S=4096,D=2048,k=0.2; attention TFLOPS % of bf16 peak"
+PUBLISHED_TOK_S = 1406304.0  # reference README.md:30, RTX 5090, same block config
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["block", "sqdk-sweep"], default="block")
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--dim", type=int, default=2048)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--sparsity", type=float, default=0.2)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    a = ap.parse_args()
+    if a.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return a
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ---------------------------------------------------------------------------
+# peaks, traffic, clocks
+# ---------------------------------------------------------------------------
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profiled_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from the committed ncu summary
+    (profiles/<kernel>__<workload>.txt, line ``dram_bytes_per_launch = N``)."""
+    path = os.path.join(REPO, "profiles", f"{kernel}__{workload}.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch"):
+                    return float(line.split("=", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="hspmn_clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, n = [], [], set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.gpus:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                n += 1
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": n}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference algorithm on host cores
+# ---------------------------------------------------------------------------
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((d.get("num_threads", 1) for d in threadpool_info()), default=1)
+        return int(n)
+    except Exception:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def cpu_block_sample(args, seconds: float, max_steps: int | None = None, warmup: int = 1):
+    """Time the numpy oracle's HSPMNBlock forward on one sequence of the
+    workload. Returns (tok/s, sample description, cores, per-step seconds)."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from hspmn_b200 import HSPMNBlock, HSPMNConfig, seed_everything
+
+    seed_everything(42)
+    cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads,
+                      sparsity_k=args.sparsity, max_seq_len=args.seq_len)
+    block = HSPMNBlock(cfg).to(torch.bfloat16)
+    params = {k: v.float().numpy() for k, v in block.state_dict().items()}
+    ts = float(block.router.target_sparsity.item())
+    g = torch.Generator().manual_seed(1000)
+    x = torch.randn(1, args.seq_len, args.dim, generator=g).to(torch.bfloat16).float().numpy()
+    eps = float(torch.finfo(torch.bfloat16).eps)
+
+    def step():
+        oracle.block_forward(params, x, args.heads, args.kv_heads, ts, cfg.rope_base, eps, noisy_dtype="bf16")
+
+    for _ in range(warmup):
+        step()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if max_steps is not None and len(times) >= max_steps:
+            break
+        if max_steps is None and time.perf_counter() - t_start >= seconds:
+            break
+    per = statistics.mean(times)
+    sample = (f"numpy oracle HSPMNBlock.forward (fp32 arithmetic on bf16-valued weights/inputs), one sequence "
+              f"S={args.seq_len} D={args.dim} per step, {len(times)} timed step(s) after {warmup} warm-up")
+    return args.seq_len / per, sample, cpu_threads(), per
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    steps = max(1, args.steps)
+    tok_s, sample, cores, per = cpu_block_sample(args, 0.0, max_steps=steps, warmup=min(args.warmup, 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": tok_s / PUBLISHED_TOK_S, "dtype": "f32",
+        "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
+        "config": workload_config(args, per_gpu_batch=1),
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def workload_config(args, per_gpu_batch=None):
+    B = args.batch if per_gpu_batch is None else per_gpu_batch
+    return {
+        "workload": (f"HSPMNBlock eval forward, bf16, dim={args.dim} heads={args.heads} kv_heads={args.kv_heads} "
+                     f"S={args.seq_len} k={args.sparsity}, {B} sequence(s) per GPU"),
+        "batch_per_gpu": B, "global_batch": B * args.gpus, "seq_len": args.seq_len, "dim": args.dim,
+        "num_heads": args.heads, "num_kv_heads": args.kv_heads, "sparsity_k": args.sparsity,
+        "parallelism": f"batch-partitioned x{args.gpus}, no data-path collective",
+        "l2": "inputs larger than L2 (x is B*S*D*2 bytes per GPU per step)",
+    }
+
+
+def init_dist(world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    return torch.device("cuda", local_rank)
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(val: float, world: int, dev) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return val
+    t = torch.tensor([val], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_block(args):
+    import torch
+
+    from hspmn_b200 import HSPMNBlock, HSPMNConfig, ops, seed_everything
+
+    rank, world, local_rank = dist_env()
+    dev = init_dist(world, local_rank)
+    seed_everything(42)
+    cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads, sparsity_k=args.sparsity,
+                      max_seq_len=args.seq_len)
+    model = HSPMNBlock(cfg).to(dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    B, S, D = args.batch, args.seq_len, args.dim
+    x = torch.randn(B, S, D, device=dev, dtype=torch.bfloat16, generator=g)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            model(x)
+        # algorithmic attention FLOPs of one forward (the indices do not change between steps)
+        idx = model.router(x).indices
+        sqdk_flops = 4.0 * cfg.head_dim * cfg.num_heads * float((idx + 1).sum().item())
+        k_sel = idx.shape[1]
+        barrier(world)
+        clocks = ClockSampler([local_rank] if world == 1 else range(world)) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        launches0 = ops.LaunchStats.launches
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ops.KernelTimer() as kt:
+            start.record()
+            for _ in range(args.steps):
+                model(x)
+            end.record()
+        torch.cuda.synchronize()
+        launches = ops.LaunchStats.launches - launches0
+        clock_info = clocks.stop() if clocks else None
+        ms_total = max_over_ranks(start.elapsed_time(end), world, dev)
+        barrier(world)
+        kres = kt.results()
+
+        # end to end through the public API: host x -> device -> forward -> host out
+        e2e = None
+        if not args.no_e2e:
+            x_host = x.cpu().pin_memory()
+            out_host = torch.empty((B, S, D), dtype=torch.bfloat16).pin_memory()
+            aux_host = torch.empty((), dtype=torch.bfloat16).pin_memory()
+            for _ in range(2):
+                out, aux = model(x_host.to(dev, non_blocking=True))
+                out_host.copy_(out, non_blocking=True)
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.e2e_steps):
+                out, aux = model(x_host.to(dev, non_blocking=True))
+                out_host.copy_(out, non_blocking=True)
+                aux_host.copy_(aux, non_blocking=True)
+            e1.record()
+            torch.cuda.synchronize()
+            e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+            e2e = {"value": B * S * args.e2e_steps * world / (e2e_ms / 1e3), "unit": "tok/s",
+                   "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                   "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + 2,
+                   "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps}
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_src = load_peaks()
+    sq = kres.get("sqdk_fwd", {"launches": 0, "ms": float("nan")})
+    sq_ms = sq["ms"] / max(1, sq["launches"])
+    achieved = sqdk_flops / (sq_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    wl_tag = f"B{B}_S{S}_D{D}_H{args.heads}_Hkv{args.kv_heads}"
+    traffic = profiled_traffic("sqdk_fwd", wl_tag)
+    esz = 2
+    kernels = {}
+    for name, r in kres.items():
+        per = r["ms"] / max(1, r["launches"])
+        kernels[name] = {"launches": r["launches"], "ms_per_launch": per}
+    if "gather_rows" in kernels:
+        gb = 2 * B * k_sel * D * esz + B * k_sel * 8
+        kernels["gather_rows"]["GB_s"] = gb / (kernels["gather_rows"]["ms_per_launch"] / 1e3) / 1e9
+    if "scatter_rows" in kernels:
+        gb = B * k_sel * D * esz + B * S * D * esz + B * k_sel * 8
+        kernels["scatter_rows"]["GB_s"] = gb / (kernels["scatter_rows"]["ms_per_launch"] / 1e3) / 1e9
+    if "router_topk" in kernels:
+        gb = B * S * esz + B * k_sel * 8 + B * S
+        kernels["router_topk"]["GB_s"] = gb / (kernels["router_topk"]["ms_per_launch"] / 1e3) / 1e9
+    if "sqdk_fwd" in kernels:
+        kernels["sqdk_fwd"]["TFLOP_s"] = achieved
+        kernels["sqdk_fwd"]["algorithmic_flops"] = sqdk_flops
+
+    value = B * S * args.steps * world / (ms_total / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
+        "config": workload_config(args),
+        "roofline": {"bound": "tensor", "kernel": "sqdk_fwd", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_src} bf16 dense, sustained (kernel timed inside a long step)",
+                     "flops_per_launch": sqdk_flops, "ms_per_launch": sq_ms, "k_selected": k_sel},
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "clocks": clock_info,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
+        tok_s, sample, cores, _ = cpu_block_sample(args, args.cpu_sample_seconds)
+        line["cpu_baseline"] = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# standalone SQDK sparsity sweep
+# ---------------------------------------------------------------------------
+
+
+def run_sweep(args):
+    import torch
+
+    from hspmn_b200 import ops
+
+    rank, world, local_rank = dist_env()
+    dev = init_dist(world, local_rank)
+    B, S, H, hd = 8, 32768, 16, 128
+    peaks, peak_src = load_peaks()
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    q = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    logits = torch.randn(B, S, device=dev, dtype=torch.float32, generator=g)
+    for frac in (0.05, 0.1, 0.2, 0.5):
+        K = max(1, int(S * frac))
+
+        def step():
+            idx, _ = ops.router_topk(logits, None, K, torch.float32)
+            qs = ops.gather_rows(q, idx)
+            o = ops.sqdk_fwd(qs, k, v, idx, hd ** -0.5)
+            return ops.scatter_rows(o, idx, S), idx
+
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                _, idx = step()
+            flops = 4.0 * hd * H * float((idx + 1).sum().item())
+            barrier(world)
+            with ops.KernelTimer() as kt:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.steps):
+                    step()
+                e1.record()
+            torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+        res = {n: r["ms"] / r["launches"] for n, r in kt.results().items()}
+        if rank == 0:
+            tf = flops / (res["sqdk_fwd"] / 1e3) / 1e12
+            gather_b = 2 * B * K * H * hd * 2 + B * K * 8
+            scatter_b = B * K * H * hd * 2 + B * S * H * hd * 2 + B * K * 8
+            print(json.dumps({
+                "metric": "standalone SQDK sweep: attention TFLOP/s and gather/scatter GB/s", "workload":
+                f"B={B} S={S} H=Hkv={H} hd={hd} k={frac} (K={K}), router on f32 logits", "n_gpus": world,
+                "value": tf, "unit": "TFLOP/s", "frac_of_peak": tf / float(peaks["bf16_tflops"]),
+                "peak_source": f"{peak_src} bf16 dense, burst", "ms_per_step": ms / args.steps,
+                "router_us": res["router_topk"] * 1e3,
+                "gather_GB_s": gather_b / (res["gather_rows"] / 1e3) / 1e9,
+                "scatter_GB_s": scatter_b / (res["scatter_rows"] / 1e3) / 1e9,
+                "hbm_peak_GB_s": float(peaks["hbm_gbs"]), "sqdk_ms": res["sqdk_fwd"]}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    _, world, _ = dist_env()
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    args.gpus = world if world > 1 else args.gpus
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.gpus > 1 and world == 1:
+        raise SystemExit("--gpus N>1 needs torchrun: python -m torch.distributed.run --nproc-per-node N bench.py ...")
+    if args.workload == "sqdk-sweep":
+        return run_sweep(args)
+    return run_block(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,78 @@
+"""Build libhspmn_sm100.so, the sm_100a CUDA library behind hspmn_b200.
+
+The library is compiled in-tree (next to the Python package) with nvcc for
+``sm_100a`` only; the product has no other target. Rebuilds only when a
+source under ``csrc/`` or ``include/`` is newer than the library.
+
+    python hspmn-v2.1_b200/build_native.py [--force] [--debug]
+"""
+
+from __future__ import annotations
+
+import argparse
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(REPO, "include")
+LIB = os.path.join(HERE, "hspmn_b200", "libhspmn_sm100.so")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-std=c++17", "-lineinfo",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-shared", "-cudart", "static",
+    "--expt-relaxed-constexpr",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found; the HSPMN library needs the CUDA toolkit to build")
+
+
+def sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+                  + glob.glob(os.path.join(INCLUDE, "*.h")))
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(LIB):
+        return False
+    t = os.path.getmtime(LIB)
+    return all(os.path.getmtime(s) <= t for s in sources())
+
+
+def build(force: bool = False, debug: bool = False, verbose: bool = False) -> str:
+    if not force and not debug and up_to_date():
+        return LIB
+    out = LIB if not debug else LIB.replace(".so", "_debug.so")
+    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC,
+           os.path.join(CSRC, "hspmn_sm100.cu"), "-o", out + ".tmp"]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    if debug:
+        cmd.insert(1, "-DHSPMN_DEBUG=1")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
+    if verbose:
+        sys.stderr.write(r.stdout + r.stderr)
+    os.replace(out + ".tmp", out)
+    return out
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--debug", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, debug=a.debug, verbose=a.verbose))

@@ -1,0 +1,308 @@
+// C ABI of libhspmn_sm100.so (declared in include/hspmn_sm100.h): argument
+// validation, launch configuration and TMA descriptor encoding for the
+// router, row gather/scatter and SQDK attention kernels. One translation unit
+// so all kernels share the device error word.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "router.cuh"
+#include "rows.cuh"
+#include "sqdk.cuh"
+
+namespace hspmn {
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+
+int g_arch_ok[kMaxDevices];  // 0 unknown, 1 sm_100, -1 other
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HSPMN_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return HSPMN_ERR_DEVICE;
+  int state = __atomic_load_n(&g_arch_ok[dev], __ATOMIC_ACQUIRE);
+  if (state == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return HSPMN_ERR_CUDA;
+    state = (major == 10 && minor == 0) ? 1 : -1;
+    __atomic_store_n(&g_arch_ok[dev], state, __ATOMIC_RELEASE);
+  }
+  return state == 1 ? HSPMN_OK : HSPMN_ERR_DEVICE;
+}
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HSPMN_OK : HSPMN_ERR_CUDA;
+}
+
+bool valid_dtype(int d) { return d == HSPMN_F32 || d == HSPMN_F16 || d == HSPMN_BF16; }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---------------------------------------------------------------------------
+// TMA descriptor encoding through the driver entry point (no libcuda link)
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4-D tiled map over a [d3][d2][d1][d0] tensor (d0 innermost, stride 1),
+// 128-byte swizzle, zero fill out of bounds. Strides in bytes.
+int encode_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[4],
+              const uint64_t strides_bytes[3], const uint32_t box[4]) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return HSPMN_ERR_CUDA;
+  cuuint64_t gd[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t gs[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, dt, 4, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HSPMN_OK : HSPMN_ERR_INVALID;
+}
+
+template <int HD, bool kBF16>
+int launch_sqdk(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const SqdkParams& prm,
+                cudaStream_t stream) {
+  using L = SqdkLayout<HD>;
+  auto kern = sqdk_fwd_kernel<HD, kBF16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
+    return HSPMN_ERR_CUDA;
+  const int64_t grid = static_cast<int64_t>(prm.T) * prm.B * prm.Hkv;
+  if (grid > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  kern<<<static_cast<unsigned>(grid), kSqdkThreads, L::kAlloc, stream>>>(mq, mk, mv, prm);
+  return launch_status();
+}
+
+template <typename V>
+void launch_gather(const void* src, int64_t ssb, int64_t sss, const int64_t* idx, int64_t isb, void* dst, int64_t dsb,
+                   int64_t dsk, int64_t B, int64_t S, int64_t K, int64_t row_bytes, cudaStream_t stream) {
+  const int64_t nrows = B * K;
+  int64_t blocks = (nrows + kRowWarps - 1) / kRowWarps;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  gather_rows_kernel<V><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+      static_cast<const char*>(src), ssb, sss, idx, isb, static_cast<char*>(dst), dsb, dsk, B, S, K,
+      row_bytes / static_cast<int64_t>(sizeof(V)));
+}
+
+template <typename V>
+void launch_scatter(const void* src, int64_t ssb, int64_t ssk, const int64_t* idx, int64_t isb, void* dst,
+                    int64_t dsb, int64_t dss, int64_t B, int64_t S, int64_t K, int64_t row_bytes,
+                    cudaStream_t stream) {
+  dim3 grid(static_cast<unsigned>((S + kScatterRowsPerCta - 1) / kScatterRowsPerCta), static_cast<unsigned>(B));
+  scatter_rows_kernel<V><<<grid, kRowThreads, 0, stream>>>(static_cast<const char*>(src), ssb, ssk, idx, isb,
+                                                           static_cast<char*>(dst), dsb, dss, S, K,
+                                                           row_bytes / static_cast<int64_t>(sizeof(V)));
+}
+
+// widest vector (16/8/4/2 bytes) every address and stride is a multiple of
+int row_vector_bytes(const void* a, const void* b, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
+                     int64_t row_bytes) {
+  uintptr_t all = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | static_cast<uintptr_t>(s0) |
+                  static_cast<uintptr_t>(s1) | static_cast<uintptr_t>(s2) | static_cast<uintptr_t>(s3) |
+                  static_cast<uintptr_t>(row_bytes);
+  for (int w = 16; w >= 2; w >>= 1)
+    if ((all % w) == 0) return w;
+  return 0;
+}
+
+}  // namespace
+}  // namespace hspmn
+
+using namespace hspmn;
+
+extern "C" {
+
+int hspmn_version(void) { return kVersion; }
+
+const char* hspmn_strerror(int status) {
+  switch (status) {
+    case HSPMN_OK: return "ok";
+    case HSPMN_ERR_INVALID: return "invalid argument (null pointer, size or shape)";
+    case HSPMN_ERR_DTYPE: return "unsupported element type";
+    case HSPMN_ERR_ALIGN: return "pointer or stride alignment not supported";
+    case HSPMN_ERR_UNSUPPORTED: return "head_dim or head grouping not supported";
+    case HSPMN_ERR_CUDA: return "CUDA runtime error or launch failure";
+    case HSPMN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    default: return "unknown status";
+  }
+}
+
+int hspmn_router_topk(const void* logits, int logits_dtype, int64_t logits_rs, const void* temp, int temp_dtype,
+                      int noisy_dtype, int64_t B, int64_t S, int64_t K, int64_t* indices, int64_t indices_rs,
+                      uint8_t* mask, int64_t mask_rs, void* stream) {
+  if (!logits || !indices || B < 0 || S <= 0 || K < 1 || K > S || S > 0x7FFFFFFF || B > 0x7FFFFFFF)
+    return HSPMN_ERR_INVALID;
+  if (!valid_dtype(logits_dtype) || !valid_dtype(noisy_dtype) || (temp && !valid_dtype(temp_dtype)))
+    return HSPMN_ERR_DTYPE;
+  if (logits_rs < S || indices_rs < K || (mask && mask_rs < S)) return HSPMN_ERR_INVALID;
+  if (B == 0) return HSPMN_OK;
+  if (int rc = check_device()) return rc;
+  const int64_t key_bytes = S * (noisy_dtype == HSPMN_F32 ? 4 : 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (key_bytes <= kRouterSmemKeyBytes) {
+    if (cudaFuncSetAttribute(router_topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRouterSmemKeyBytes) != cudaSuccess)
+      return HSPMN_ERR_CUDA;
+    router_topk_kernel<true><<<static_cast<unsigned>(B), kRouterThreads, static_cast<size_t>(key_bytes), st>>>(
+        logits, logits_dtype, logits_rs, temp, temp_dtype, noisy_dtype, static_cast<int>(S), static_cast<int>(K),
+        indices, indices_rs, mask, mask_rs);
+  } else {
+    router_topk_kernel<false><<<static_cast<unsigned>(B), kRouterThreads, 0, st>>>(
+        logits, logits_dtype, logits_rs, temp, temp_dtype, noisy_dtype, static_cast<int>(S), static_cast<int>(K),
+        indices, indices_rs, mask, mask_rs);
+  }
+  return launch_status();
+}
+
+int hspmn_gather_rows(const void* src, int64_t src_sb, int64_t src_ss, const int64_t* idx, int64_t idx_sb,
+                      void* dst, int64_t dst_sb, int64_t dst_sk, int64_t B, int64_t S, int64_t K, int64_t row_bytes,
+                      void* stream) {
+  if (!src || !idx || !dst || B < 0 || S < 1 || K < 0 || row_bytes <= 0) return HSPMN_ERR_INVALID;
+  if (src_sb < 0 || src_ss < 0 || dst_sb < 0 || dst_sk < 0 || idx_sb < K) return HSPMN_ERR_INVALID;
+  if (B == 0 || K == 0) return HSPMN_OK;
+  const int vec = row_vector_bytes(src, dst, src_sb, src_ss, dst_sb, dst_sk, row_bytes);
+  if (vec == 0) return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (vec) {
+    case 16: launch_gather<uint4>(src, src_sb, src_ss, idx, idx_sb, dst, dst_sb, dst_sk, B, S, K, row_bytes, st); break;
+    case 8: launch_gather<uint2>(src, src_sb, src_ss, idx, idx_sb, dst, dst_sb, dst_sk, B, S, K, row_bytes, st); break;
+    case 4: launch_gather<unsigned>(src, src_sb, src_ss, idx, idx_sb, dst, dst_sb, dst_sk, B, S, K, row_bytes, st); break;
+    case 2: launch_gather<unsigned short>(src, src_sb, src_ss, idx, idx_sb, dst, dst_sb, dst_sk, B, S, K, row_bytes, st); break;
+    default: return HSPMN_ERR_ALIGN;
+  }
+  return launch_status();
+}
+
+int hspmn_scatter_rows(const void* src, int64_t src_sb, int64_t src_sk, const int64_t* idx, int64_t idx_sb,
+                       void* dst, int64_t dst_sb, int64_t dst_ss, int64_t B, int64_t S, int64_t K, int64_t row_bytes,
+                       void* stream) {
+  if (!dst || B < 0 || S < 1 || K < 0 || row_bytes <= 0 || K > S) return HSPMN_ERR_INVALID;
+  if ((K > 0 && (!src || !idx || idx_sb < K)) || src_sb < 0 || src_sk < 0 || dst_sb < 0 || dst_ss < 0)
+    return HSPMN_ERR_INVALID;
+  if (B == 0) return HSPMN_OK;
+  if (B > 65535) return HSPMN_ERR_INVALID;
+  const int vec = row_vector_bytes(src ? src : dst, dst, src_sb, src_sk, dst_sb, dst_ss, row_bytes);
+  if (vec == 0) return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (vec) {
+    case 16: launch_scatter<uint4>(src, src_sb, src_sk, idx, idx_sb, dst, dst_sb, dst_ss, B, S, K, row_bytes, st); break;
+    case 8: launch_scatter<uint2>(src, src_sb, src_sk, idx, idx_sb, dst, dst_sb, dst_ss, B, S, K, row_bytes, st); break;
+    case 4: launch_scatter<unsigned>(src, src_sb, src_sk, idx, idx_sb, dst, dst_sb, dst_ss, B, S, K, row_bytes, st); break;
+    case 2: launch_scatter<unsigned short>(src, src_sb, src_sk, idx, idx_sb, dst, dst_sb, dst_ss, B, S, K, row_bytes, st); break;
+    default: return HSPMN_ERR_ALIGN;
+  }
+  return launch_status();
+}
+
+int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                   const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
+                   const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
+                   int dtype, float sm_scale, void* stream) {
+  if (!q || !k || !v || !idx || !o || !qs || !ks || !vs || !os) return HSPMN_ERR_INVALID;
+  if (B < 0 || K < 0 || S < 1 || H < 1 || Hkv < 1 || !(sm_scale > 0.0f) || !std::isfinite(sm_scale))
+    return HSPMN_ERR_INVALID;
+  if (dtype != HSPMN_BF16 && dtype != HSPMN_F16) return HSPMN_ERR_DTYPE;
+  if (hd < 8 || hd > 128 || hd % 8 != 0) return HSPMN_ERR_UNSUPPORTED;
+  if (H % Hkv != 0 || H / Hkv > kSqdkBM) return HSPMN_ERR_UNSUPPORTED;
+  if (B == 0 || K == 0) return HSPMN_OK;
+  if (B > 0x7FFFFFFF || K > 0x7FFFFFFF || S > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  const int64_t es = 2;
+  if (qs[3] != 1 || ks[3] != 1 || vs[3] != 1 || os[3] != 1) return HSPMN_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i) {
+    if ((qs[i] * es) % 16 || (ks[i] * es) % 16 || (vs[i] * es) % 16 || (os[i] * es) % 16) return HSPMN_ERR_ALIGN;
+    if (qs[i] <= 0 || ks[i] <= 0 || vs[i] <= 0 || os[i] <= 0) return HSPMN_ERR_INVALID;
+  }
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16)) return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+
+  const int G = static_cast<int>(H / Hkv);
+  const int QT = kSqdkBM / G;
+  const int64_t T = (K + QT - 1) / QT;
+  const CUtensorMapDataType dt =
+      dtype == HSPMN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+
+  CUtensorMap mq, mk, mv;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(H), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(B)};
+    const uint64_t str[3] = {static_cast<uint64_t>(qs[2] * es), static_cast<uint64_t>(qs[1] * es),
+                             static_cast<uint64_t>(qs[0] * es)};
+    const uint32_t box[4] = {64u, static_cast<uint32_t>(G), static_cast<uint32_t>(QT), 1u};
+    if (int rc = encode_4d(&mq, q, dt, dims, str, box)) return rc;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(Hkv), static_cast<uint64_t>(S),
+                              static_cast<uint64_t>(B)};
+    const uint32_t box[4] = {64u, 1u, static_cast<uint32_t>(kSqdkBN), 1u};
+    const uint64_t sk[3] = {static_cast<uint64_t>(ks[2] * es), static_cast<uint64_t>(ks[1] * es),
+                            static_cast<uint64_t>(ks[0] * es)};
+    const uint64_t sv[3] = {static_cast<uint64_t>(vs[2] * es), static_cast<uint64_t>(vs[1] * es),
+                            static_cast<uint64_t>(vs[0] * es)};
+    if (int rc = encode_4d(&mk, k, dt, dims, sk, box)) return rc;
+    if (int rc = encode_4d(&mv, v, dt, dims, sv, box)) return rc;
+  }
+  SqdkParams prm;
+  prm.idx = idx;
+  prm.hd = static_cast<int>(hd);
+  prm.idx_sb = idx_sb;
+  prm.idx_sk = idx_sk;
+  prm.o = o;
+  prm.o_sb = os[0];
+  prm.o_sk = os[1];
+  prm.o_sh = os[2];
+  prm.B = static_cast<int>(B);
+  prm.K = static_cast<int>(K);
+  prm.S = static_cast<int>(S);
+  prm.H = static_cast<int>(H);
+  prm.Hkv = static_cast<int>(Hkv);
+  prm.G = G;
+  prm.QT = QT;
+  prm.T = static_cast<int>(T);
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (hd > 64)
+    return dtype == HSPMN_BF16 ? launch_sqdk<128, true>(mq, mk, mv, prm, st) : launch_sqdk<128, false>(mq, mk, mv, prm, st);
+  return dtype == HSPMN_BF16 ? launch_sqdk<64, true>(mq, mk, mv, prm, st) : launch_sqdk<64, false>(mq, mk, mv, prm, st);
+}
+
+int hspmn_device_errors(unsigned* bits, int clear, void* stream) {
+  if (!bits) return HSPMN_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return HSPMN_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(bits, g_device_errors, sizeof(unsigned)) != cudaSuccess) return HSPMN_ERR_CUDA;
+  if (clear) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_device_errors, &zero, sizeof(unsigned)) != cudaSuccess) return HSPMN_ERR_CUDA;
+  }
+  return HSPMN_OK;
+}
+
+}  // extern "C"

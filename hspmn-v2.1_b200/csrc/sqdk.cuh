@@ -1,0 +1,366 @@
+// Sparse-query dense-key causal attention on tcgen05 / TMEM / TMA (sm_100a).
+//
+// Replaces _sqdk_fwd_kernel (kernels_v2_1.py:11-139) with the grouped-head
+// semantics of the reference's Flex path (hspmn_v2_1.py:212).
+//
+// Head dims up to 128 (multiples of 8) run on a 64- or 128-wide tile: the TMA
+// boxes are always 64 columns wide and zero-fill the columns past head_dim,
+// which add nothing to Q K^T and produce zero O columns that are not stored.
+//
+// Work unit ("tile"): one sequence b, one K/V head g and QT = 128 / G
+// consecutive selected queries together with the G query heads that read
+// head g, i.e. 128 rows (query, head) that all share the same K/V blocks.
+// Rows are ordered r = q * G + h, exactly the order a TMA box over the
+// [B,K,H,hd] query tensor lands in shared memory.
+//
+// Per tile the key loop runs over 64-key blocks up to the largest position in
+// the tile (indices are sorted, so tiles near the end of the sequence are the
+// long ones and are launched first). Each block:
+//   S  = Q K^T        tcgen05.mma SS, M=128 N=64 K=hd, S in TMEM (2 buffers)
+//   P  = exp2(S*c - m) softmax warps: one thread per row, TMEM -> registers,
+//                     causal mask on the diagonal blocks, P written back to
+//                     TMEM as bf16/f16 over the S buffer it came from
+//   O += P V          tcgen05.mma TS, A = P from TMEM, B = V (MN-major smem)
+// O stays in TMEM for the whole tile; it is rescaled only when a row's
+// running maximum grows by more than 2^8 (lazy rescaling), which with
+// fp32 accumulation is exact up to rounding.
+//
+// Warp roles (192 threads, two CTAs per SM):
+//   warp 0      TMA producer: Q once, then K_j / V_j through 2-stage rings
+//   warp 1      TMEM allocation + single-thread MMA issue
+//   warps 2..5  softmax, lazy O correction, epilogue (row = TMEM lane)
+// Every mbarrier wait is bounded (common.cuh); a wait that gives up flags
+// HSPMN_DEVERR_TIMEOUT, tells the other roles to stop, drains what this CTA
+// has in flight and frees its tensor memory before returning.
+#pragma once
+
+#include "common.cuh"
+
+namespace hspmn {
+
+constexpr int kSqdkBM = 128;       // rows per tile
+constexpr int kSqdkBN = 64;        // keys per block
+constexpr int kSqdkStages = 2;     // depth of the K ring and of the V ring
+constexpr int kSqdkThreads = 192;  // 6 warps
+constexpr float kRescaleLog2 = 8.0f;
+
+template <int HD>
+struct SqdkLayout {
+  static constexpr int kChunks = HD / 64;                    // 128-byte column chunks per row
+  static constexpr int kQChunkBytes = kSqdkBM * 128;         // 16 KB
+  static constexpr int kKVChunkBytes = kSqdkBN * 128;        // 8 KB
+  static constexpr int kKVBytes = kChunks * kKVChunkBytes;   // one K or V block
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kChunks * kQChunkBytes;
+  static constexpr int kVOff = kKOff + kSqdkStages * kKVBytes;
+  static constexpr int kBytes = kVOff + kSqdkStages * kKVBytes;
+  static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
+  static constexpr uint32_t kTmemCols = 256;    // S0 | S1 | O
+  static constexpr int kOCol = 2 * kSqdkBN;
+  static_assert(kOCol + HD <= static_cast<int>(kTmemCols), "TMEM budget");
+};
+
+struct SqdkParams {
+  const int64_t* idx;
+  int hd;  // real head_dim (<= the padded tile width HD)
+  int64_t idx_sb, idx_sk;
+  void* o;
+  int64_t o_sb, o_sk, o_sh;  // elements
+  int B, K, S, H, Hkv, G, QT, T;
+  float scale_log2;
+};
+
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Wait used only while tearing down: ignores the abort flag, keeps the limit.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0; it < kWaitLimitIters; ++it) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  raise_device_error(HSPMN_DEVERR_TIMEOUT);
+}
+
+template <int HD, bool kBF16>
+__global__ void __launch_bounds__(kSqdkThreads, 2)
+    sqdk_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const SqdkParams p) {
+  using L = SqdkLayout<HD>;
+  extern __shared__ uint8_t sqdk_smem_raw[];
+  __shared__ __align__(8) uint64_t bar_q;
+  __shared__ __align__(8) uint64_t bar_kfull[kSqdkStages], bar_kempty[kSqdkStages];
+  __shared__ __align__(8) uint64_t bar_vfull[kSqdkStages], bar_vempty[kSqdkStages];
+  __shared__ __align__(8) uint64_t bar_sfull[2], bar_pfull[2];
+  __shared__ __align__(8) uint64_t bar_odone, bar_ofinal, bar_drain;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int tile_maxpos;
+  __shared__ volatile uint32_t abort_flag;
+
+  const uint32_t sbase = (smem_u32(sqdk_smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // tile coordinates: all (b, g) pairs of the last query tile first
+  const int BG = p.B * p.Hkv;
+  const int t = p.T - 1 - static_cast<int>(blockIdx.x) / BG;
+  const int bg = static_cast<int>(blockIdx.x) % BG;
+  const int b = bg / p.Hkv, g = bg % p.Hkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_q, 1);
+    for (int s = 0; s < kSqdkStages; ++s) {
+      mbar_init(&bar_kfull[s], 1);
+      mbar_init(&bar_kempty[s], 1);
+      mbar_init(&bar_vfull[s], 1);
+      mbar_init(&bar_vempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_sfull[s], 1);
+      mbar_init(&bar_pfull[s], 4);  // one arrival per softmax warp
+    }
+    mbar_init(&bar_odone, 1);
+    mbar_init(&bar_ofinal, 1);
+    mbar_init(&bar_drain, 1);
+    tile_maxpos = -1;
+    abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, L::kTmemCols);
+    tmem_relinquish();
+  }
+
+  // softmax rows: which (query, head) this thread owns and its position
+  int pos = -1, qi = 0, hh = 0;
+  bool row_valid = false;
+  if (warp >= 2) {
+    const int r = 32 * (warp & 3) + lane;
+    const int qloc = r / p.G;
+    qi = t * p.QT + qloc;
+    hh = g * p.G + (r - qloc * p.G);
+    if (qloc < p.QT && qi < p.K) {
+      int64_t ps = __ldg(p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk);
+      row_valid = true;
+      if (ps < 0 || ps >= p.S) {
+        raise_device_error(HSPMN_DEVERR_POSITION);
+        ps = ps < 0 ? -1 : p.S - 1;
+      }
+      pos = static_cast<int>(ps);
+    }
+    const int wmax = __reduce_max_sync(0xFFFFFFFFu, pos);
+    if (lane == 0) atomicMax(&tile_maxpos, wmax);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int nblk = tile_maxpos < 0 ? 0 : tile_maxpos / kSqdkBN + 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nblk > 0) {
+      mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(L::kChunks * p.G * p.QT * 128));
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_4d(sbase + L::kQOff + c * L::kQChunkBytes, &tmQ, &bar_q, c * 64, g * p.G, t * p.QT, b);
+      int nk = 0, nv = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % kSqdkStages, r = j / kSqdkStages;
+        if (r > 0 && !mbar_wait(&bar_kempty[s], (r - 1) & 1, &abort_flag)) break;
+        mbar_arrive_expect_tx(&bar_kfull[s], L::kKVBytes);
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sbase + L::kKOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmK, &bar_kfull[s], c * 64, g,
+                      j * kSqdkBN, b);
+        ++nk;
+        if (r > 0 && !mbar_wait(&bar_vempty[s], (r - 1) & 1, &abort_flag)) break;
+        mbar_arrive_expect_tx(&bar_vfull[s], L::kKVBytes);
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sbase + L::kVOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmV, &bar_vfull[s], c * 64, g,
+                      j * kSqdkBN, b);
+        ++nv;
+      }
+      // every copy this thread issued has landed before the CTA may exit
+      mbar_wait_drain(&bar_q, 0);
+      for (int s = 0; s < kSqdkStages; ++s) {
+        if (nk > s) mbar_wait_drain(&bar_kfull[s], ((nk - 1 - s) / kSqdkStages) & 1);
+        if (nv > s) mbar_wait_drain(&bar_vfull[s], ((nv - 1 - s) / kSqdkStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0 && nblk > 0) {
+      constexpr int kAB = kBF16 ? 1 : 0;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kSqdkBM, kSqdkBN, kAB, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kSqdkBM, HD, kAB, false, true);
+      const uint32_t tO = tmem + L::kOCol;
+      bool ok = mbar_wait(&bar_q, 0, &abort_flag);
+      tc_fence_after();
+      auto issue_pv = [&](int jj) -> bool {
+        const int s = jj % kSqdkStages, r = jj / kSqdkStages, sb = jj & 1;
+        if (!mbar_wait(&bar_pfull[sb], (jj >> 1) & 1, &abort_flag)) return false;
+        if (!mbar_wait(&bar_vfull[s], r & 1, &abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t vb = sbase + L::kVOff + s * L::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kSqdkBN / 16; ++kk) {
+          // V block, MN-major: 16 keys = 2 groups of 8 rows (SBO 1024 B),
+          // hd in 64-column chunks L::kKVChunkBytes apart (LBO)
+          const uint64_t bdesc = sw128_desc(vb + kk * 16 * 128, L::kKVChunkBytes, 1024);
+          umma_ts(tO, tmem + sb * kSqdkBN + kk * 8, bdesc, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bar_vempty[s]);
+        umma_commit(&bar_odone);
+        return true;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
+        if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kb = sbase + L::kKOff + s * L::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int c = kk >> 2, w = kk & 3;  // 64-column chunk, 32-byte step inside the swizzle row
+          const uint64_t adesc = sw128_desc(sbase + L::kQOff + c * L::kQChunkBytes + w * 32, 16, 1024);
+          const uint64_t bdesc = sw128_desc(kb + c * L::kKVChunkBytes + w * 32, 16, 1024);
+          umma_ss(tmem + sb * kSqdkBN, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar_sfull[sb]);
+        umma_commit(&bar_kempty[s]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok) ok = issue_pv(nblk - 1);
+      if (ok) umma_commit(&bar_ofinal);
+      umma_commit(&bar_drain);
+      mbar_wait_drain(&bar_drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t tS = tmem + lane_base;
+    const uint32_t tO = tmem + lane_base + L::kOCol;
+    const float c2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = nblk > 0;
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_sfull[sb], (j >> 1) & 1, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[kSqdkBN];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS + sb * kSqdkBN, r0);
+        tmem_ld32(tS + sb * kSqdkBN + 32, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = __uint_as_float(r0[i]);
+          sv[32 + i] = __uint_as_float(r1[i]);
+        }
+      }
+      const int lim = pos - j * kSqdkBN;  // columns <= lim are visible to this row
+      if (lim < kSqdkBN - 1) {
+#pragma unroll
+        for (int c = 0; c < kSqdkBN; ++c) sv[c] = (c <= lim) ? sv[c] : -INFINITY;
+      }
+      float mx = sv[0];
+#pragma unroll
+      for (int c = 1; c < kSqdkBN; ++c) mx = fmaxf(mx, sv[c]);
+      const float m_new = fmaxf(m_run, mx * c2);
+      const bool grow = m_new > m_run + kRescaleLog2;
+      const bool need_o = grow && (m_run != -INFINITY);
+      if (__any_sync(0xFFFFFFFFu, need_o)) {
+        // O holds P_0..P_{j-1} V; PV of block j-1 must have landed first
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_odone, (j - 1) & 1, &abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const float alpha = need_o ? fast_exp2(m_run - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tO + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + c, r);
+        }
+        tmem_wait_st();
+      }
+      if (grow) {
+        l_run *= fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
+      uint32_t pk[kSqdkBN / 2];
+      float lsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kSqdkBN; c += 2) {
+        const float p0 = fast_exp2(fmaf(sv[c], c2, neg_m));
+        const float p1 = fast_exp2(fmaf(sv[c + 1], c2, neg_m));
+        lsum += p0 + p1;
+        pk[c >> 1] = pack2<kBF16>(p0, p1);
+      }
+      l_run += lsum;
+      tmem_st32(tS + sb * kSqdkBN, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_pfull[sb]);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_ofinal, 0, &abort_flag));
+    using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+    Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
+                static_cast<int64_t>(hh) * p.o_sh;
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l_run;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tO + c, r);
+        tmem_wait_ld();
+        if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (c + 8 * v >= p.hd) break;
+            uint4 w;
+            w.x = pack2<kBF16>(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            w.y = pack2<kBF16>(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            w.z = pack2<kBF16>(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            w.w = pack2<kBF16>(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            dst[v] = w;
+          }
+        }
+      }
+    } else if (nblk == 0 && row_valid) {
+      // every position in the tile was negative: softmax over nothing
+      const uint32_t nanw = pack2<kBF16>(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000));
+      uint4* dst = reinterpret_cast<uint4*>(orow);
+      for (int v = 0; v < p.hd / 8; ++v) dst[v] = make_uint4(nanw, nanw, nanw, nanw);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace hspmn

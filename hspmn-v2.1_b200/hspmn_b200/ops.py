@@ -1,0 +1,317 @@
+"""torch-facing operators over the native library.
+
+Each operator is a ``torch.library`` custom op (namespace ``hspmn``) with a
+fake implementation, so ``torch.compile`` traces through it without a graph
+break. All of them run on the caller's current CUDA stream, allocate their
+outputs with the PyTorch caching allocator and never synchronise. CPU
+tensors, a missing library or a non-B200 device raise: there is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _native as N
+
+_DTYPE_CODE = {torch.float32: N.HSPMN_F32, torch.float16: N.HSPMN_F16, torch.bfloat16: N.HSPMN_BF16}
+_CODE_DTYPE = {v: k for k, v in _DTYPE_CODE.items()}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise TypeError(f"hspmn: unsupported dtype {dt}; expected float32, float16 or bfloat16") from None
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                "hspmn: the sm_100a kernels need CUDA tensors (there is no CPU path); got a tensor on "
+                f"{t.device}")
+        if t.device != dev:
+            raise RuntimeError(f"hspmn: tensors on different devices ({dev} vs {t.device})")
+    return dev
+
+
+def _stream(dev: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+class _on_device:
+    """Make ``dev`` current for the native call (the library launches on the
+    current device)."""
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev.index:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+class LaunchStats:
+    """Counts native kernel launches and, while a ``KernelTimer`` is active,
+    records CUDA events around each one on the launching stream."""
+
+    launches = 0
+    timer = None
+
+
+class KernelTimer:
+    """Context manager: per-op CUDA-event timing of the native launches made
+    inside it. ``results()`` (after a synchronize) gives, per op name, the
+    launch count and the summed device milliseconds."""
+
+    def __init__(self):
+        self.events = {}
+
+    def __enter__(self):
+        LaunchStats.timer = self
+        return self
+
+    def __exit__(self, *exc):
+        LaunchStats.timer = None
+        return False
+
+    def _begin(self, name: str, dev: torch.device):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        return ev
+
+    def _end(self, name: str, dev: torch.device, start):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        self.events.setdefault(name, []).append((start, ev))
+
+    def results(self):
+        out = {}
+        for name, pairs in self.events.items():
+            ms = sum(a.elapsed_time(b) for a, b in pairs)
+            out[name] = {"launches": len(pairs), "ms": ms}
+        return out
+
+
+class _launch:
+    """Wraps one native call: counts it and times it when a timer is active."""
+
+    __slots__ = ("name", "dev", "start")
+
+    def __init__(self, name: str, dev: torch.device):
+        self.name, self.dev, self.start = name, dev, None
+
+    def __enter__(self):
+        t = LaunchStats.timer
+        if t is not None:
+            self.start = t._begin(self.name, self.dev)
+
+    def __exit__(self, exc_type, *exc):
+        if exc_type is None:
+            LaunchStats.launches += 1
+            t = LaunchStats.timer
+            if t is not None and self.start is not None:
+                t._end(self.name, self.dev, self.start)
+        return False
+
+
+def _rows_view(t: torch.Tensor, lead: int) -> Tuple[torch.Tensor, int]:
+    """View ``t`` as [lead dims..., row] with densely packed rows; copies when
+    the trailing dims are not one dense block. Returns (tensor, row_bytes)."""
+    row_elems = 1
+    for d in t.shape[lead:]:
+        row_elems *= d
+    expect = 1
+    dense = True
+    for d, s in zip(reversed(t.shape[lead:]), reversed(t.stride()[lead:])):
+        if d != 1 and s != expect:
+            dense = False
+            break
+        expect *= d
+    if not dense:
+        t = t.contiguous()
+    return t, row_elems * t.element_size()
+
+
+# ---------------------------------------------------------------------------
+# router top-K
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("hspmn::router_topk", mutates_args=())
+def router_topk(logits: torch.Tensor, temp: Optional[torch.Tensor], k: int,
+                noisy_dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Selection step of TopKRouter.forward (hspmn_v2_1.py:104-105,112-120).
+
+    ``noisy = (logits / temp)`` rounded to ``noisy_dtype`` (``temp`` a
+    one-element tensor, or None for no division); per row the ``k`` largest
+    noisy values (NaN largest, equal values: lower position first). Returns
+    (indices int64 [B,k] ascending, mask bool [B,S])."""
+    dev = _require_cuda(logits) if temp is None else _require_cuda(logits, temp)
+    if logits.dim() != 2:
+        raise ValueError(f"router_topk: logits must be [B,S], got {tuple(logits.shape)}")
+    B, S = logits.shape
+    if not (1 <= k <= S):
+        raise ValueError(f"router_topk: k={k} outside [1, S={S}]")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    if temp is not None and temp.numel() != 1:
+        raise ValueError("router_topk: temp must hold one element")
+    indices = torch.empty((B, k), dtype=torch.int64, device=dev)
+    mask = torch.empty((B, S), dtype=torch.bool, device=dev)
+    with _on_device(dev), _launch("router_topk", dev):
+        rc = N.lib().hspmn_router_topk(
+            ctypes.c_void_p(logits.data_ptr()), dtype_code(logits.dtype), logits.stride(0),
+            ctypes.c_void_p(temp.data_ptr() if temp is not None else 0),
+            dtype_code(temp.dtype) if temp is not None else 0, dtype_code(noisy_dtype),
+            B, S, k, ctypes.c_void_p(indices.data_ptr()), k, ctypes.c_void_p(mask.data_ptr()), S,
+            _stream(dev))
+        N.check(rc, "hspmn_router_topk")
+    return indices, mask
+
+
+@router_topk.register_fake
+def _(logits, temp, k, noisy_dtype):
+    B, S = logits.shape
+    return (logits.new_empty((B, k), dtype=torch.int64), logits.new_empty((B, S), dtype=torch.bool))
+
+
+# ---------------------------------------------------------------------------
+# gather / scatter of selected rows
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("hspmn::gather_rows", mutates_args=())
+def gather_rows(src: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    """``out[b,i,...] = src[b, indices[b,i], ...]`` (hspmn_v2_1.py:185-186).
+
+    ``src`` is [B,S,...]; each position's trailing dims form one row. The
+    result is a new contiguous [B,K,...] tensor."""
+    dev = _require_cuda(src, indices)
+    if indices.dim() != 2 or indices.dtype != torch.int64 or indices.shape[0] != src.shape[0]:
+        raise ValueError("gather_rows: indices must be int64 [B,K] matching src's batch")
+    if indices.stride(1) != 1:
+        indices = indices.contiguous()
+    B, S = src.shape[0], src.shape[1]
+    K = indices.shape[1]
+    src, row_bytes = _rows_view(src, 2)
+    out = torch.empty((B, K) + tuple(src.shape[2:]), dtype=src.dtype, device=dev)
+    es = src.element_size()
+    with _on_device(dev), _launch("gather_rows", dev):
+        rc = N.lib().hspmn_gather_rows(
+            ctypes.c_void_p(src.data_ptr()), src.stride(0) * es, src.stride(1) * es,
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0),
+            ctypes.c_void_p(out.data_ptr()), K * row_bytes, row_bytes, B, S, K, row_bytes, _stream(dev))
+        N.check(rc, "hspmn_gather_rows")
+    return out
+
+
+@gather_rows.register_fake
+def _(src, indices):
+    return src.new_empty((src.shape[0], indices.shape[1]) + tuple(src.shape[2:]))
+
+
+@torch.library.custom_op("hspmn::scatter_rows", mutates_args=())
+def scatter_rows(src: torch.Tensor, indices: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """``out = zeros([B,seq_len,...]); out[b, indices[b,i]] = src[b,i]``
+    (hspmn_v2_1.py:195-196) in a single pass over ``out``.
+
+    ``indices`` rows must be strictly ascending, as the router emits them."""
+    dev = _require_cuda(src, indices)
+    if indices.dim() != 2 or indices.dtype != torch.int64 or tuple(indices.shape) != tuple(src.shape[:2]):
+        raise ValueError("scatter_rows: indices must be int64 [B,K] matching src[:2]")
+    if indices.stride(1) != 1:
+        indices = indices.contiguous()
+    B, K = indices.shape
+    src, row_bytes = _rows_view(src, 2)
+    out = torch.empty((B, seq_len) + tuple(src.shape[2:]), dtype=src.dtype, device=dev)
+    es = src.element_size()
+    with _on_device(dev), _launch("scatter_rows", dev):
+        rc = N.lib().hspmn_scatter_rows(
+            ctypes.c_void_p(src.data_ptr()), src.stride(0) * es, src.stride(1) * es,
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0),
+            ctypes.c_void_p(out.data_ptr()), seq_len * row_bytes, row_bytes, B, seq_len, K, row_bytes,
+            _stream(dev))
+        N.check(rc, "hspmn_scatter_rows")
+    return out
+
+
+@scatter_rows.register_fake
+def _(src, indices, seq_len):
+    return src.new_empty((src.shape[0], seq_len) + tuple(src.shape[2:]))
+
+
+# ---------------------------------------------------------------------------
+# SQDK attention
+# ---------------------------------------------------------------------------
+
+
+def _sqdk_operand(t: torch.Tensor) -> torch.Tensor:
+    es = t.element_size()
+    if t.stride(-1) != 1 or any((s * es) % 16 for s in t.stride()[:-1]) or t.data_ptr() % 16:
+        t = t.contiguous()
+    return t
+
+
+@torch.library.custom_op("hspmn::sqdk_fwd", mutates_args=())
+def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+             sm_scale: float) -> torch.Tensor:
+    """Sparse-query dense-key causal attention (kernels_v2_1.py:11-180).
+
+    q [B,K,H,hd]; k, v [B,S,Hkv,hd] with H % Hkv == 0 (query head h reads
+    K/V head h // (H // Hkv)); indices int64 [B,K] original positions. Returns
+    o [B,K,H,hd] in q's dtype. bf16/f16 run natively; float32 operands are
+    rounded to bf16 for the tensor cores and the result is returned as float32."""
+    dev = _require_cuda(q, k, v, indices)
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("sqdk_fwd: q, k, v must be 4-D ([B,K,H,hd] / [B,S,Hkv,hd])")
+    B, K, H, hd = q.shape
+    S, Hkv = k.shape[1], k.shape[2]
+    if tuple(v.shape) != tuple(k.shape) or k.shape[0] != B or k.shape[3] != hd:
+        raise ValueError(f"sqdk_fwd: shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if tuple(indices.shape) != (B, K) or indices.dtype != torch.int64:
+        raise ValueError("sqdk_fwd: indices must be int64 [B,K]")
+    if H % Hkv != 0:
+        raise ValueError(f"sqdk_fwd: num_heads {H} is not a multiple of num_kv_heads {Hkv}")
+    out_dtype = q.dtype
+    if q.dtype == torch.float32:
+        q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"sqdk_fwd: q/k/v dtypes {q.dtype}/{k.dtype}/{v.dtype} unsupported")
+    q, k, v = _sqdk_operand(q), _sqdk_operand(k), _sqdk_operand(v)
+    o = torch.empty((B, K, H, hd), dtype=q.dtype, device=dev)
+    with _on_device(dev), _launch("sqdk_fwd", dev):
+        rc = N.lib().hspmn_sqdk_fwd(
+            ctypes.c_void_p(q.data_ptr()), N.i64_array(q.stride()),
+            ctypes.c_void_p(k.data_ptr()), N.i64_array(k.stride()),
+            ctypes.c_void_p(v.data_ptr()), N.i64_array(v.stride()),
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0), indices.stride(1),
+            ctypes.c_void_p(o.data_ptr()), N.i64_array(o.stride()),
+            B, K, S, H, Hkv, hd, dtype_code(q.dtype), float(sm_scale), _stream(dev))
+        N.check(rc, "hspmn_sqdk_fwd")
+    return o if o.dtype == out_dtype else o.to(out_dtype)
+
+
+@sqdk_fwd.register_fake
+def _(q, k, v, indices, sm_scale):
+    return torch.empty_like(q, memory_format=torch.contiguous_format)
+
+
+def device_errors(device: Optional[torch.device] = None, clear: bool = True) -> int:
+    """Synchronise the current stream of ``device`` and return (and clear)
+    the library's device flag word (``_native.DEVERR_*`` bits)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with _on_device(dev):
+        return N.device_errors(torch.cuda.current_stream(dev).cuda_stream, clear)

@@ -1,0 +1,134 @@
+/*
+ * hspmn_sm100.h - C ABI of libhspmn_sm100.so, the B200 (sm_100a) kernels of
+ * the HSPMN v2.1 contextual-stream inference path:
+ *
+ *   router top-K  ->  gather selected queries  ->  SQDK causal attention
+ *                 ->  scatter back into the [B,S,D] stream
+ *
+ * Conventions
+ *   - All buffers are device memory allocated by the caller; the library never
+ *     allocates and never synchronises the stream it is given.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Functions return HSPMN_OK (0) or a negative HSPMN_ERR_* code; the
+ *     launch is skipped when validation fails.
+ *   - Faults the host cannot see without a sync (query positions out of
+ *     range, unsorted indices given to the scatter, a pipeline wait that gave
+ *     up) set bits in a per-device flag word read by hspmn_device_errors().
+ *   - Strides are in ELEMENTS for typed tensors and in BYTES for the
+ *     row-copy kernels (gather/scatter move opaque rows).
+ *
+ * Element types: HSPMN_F32, HSPMN_F16, HSPMN_BF16.
+ */
+#ifndef HSPMN_SM100_H_
+#define HSPMN_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HSPMN_API __attribute__((visibility("default")))
+#else
+#define HSPMN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum hspmn_dtype { HSPMN_F32 = 0, HSPMN_F16 = 1, HSPMN_BF16 = 2 };
+
+enum hspmn_status {
+  HSPMN_OK = 0,
+  HSPMN_ERR_INVALID = -1,     /* null pointer, bad size or shape */
+  HSPMN_ERR_DTYPE = -2,       /* element type not supported by this entry point */
+  HSPMN_ERR_ALIGN = -3,       /* pointer / stride alignment the kernel needs */
+  HSPMN_ERR_UNSUPPORTED = -4, /* head_dim or head grouping outside the kernel's range */
+  HSPMN_ERR_CUDA = -5,        /* a CUDA runtime call or the launch failed */
+  HSPMN_ERR_DEVICE = -6       /* current device is not an sm_100 part */
+};
+
+/* bits of the device-side flag word */
+#define HSPMN_DEVERR_POSITION 1u /* a query/selected position outside [0, S) */
+#define HSPMN_DEVERR_UNSORTED 2u /* scatter indices not strictly ascending */
+#define HSPMN_DEVERR_TIMEOUT 4u  /* a bounded pipeline wait in attention gave up */
+
+/* Library version, major*10000 + minor*100 + patch. */
+HSPMN_API int hspmn_version(void);
+
+/* Static text for a status code. */
+HSPMN_API const char* hspmn_strerror(int status);
+
+/*
+ * Router selection. Replaces the eval-mode part of TopKRouter.forward,
+ * hspmn_v2_1.py:98,104-105,112-120:
+ *   noisy[b,s] = round_to(noisy_dtype, logits[b,s] / temp)
+ *   keep the K largest noisy values of each row (NaN largest; equal values:
+ *   lower position first), write their positions ascending into
+ *   indices[b, 0..K) and mask[b,s] = 1 if s was kept else 0.
+ * logits: [B,S] of logits_dtype, row stride logits_rs (elements).
+ * temp: one element of temp_dtype in device memory, or NULL for 1.
+ * indices: int64 [B,K], row stride indices_rs. mask: uint8 [B,S], row
+ * stride mask_rs; may be NULL.
+ */
+HSPMN_API int hspmn_router_topk(const void* logits, int logits_dtype, int64_t logits_rs,
+                      const void* temp, int temp_dtype, int noisy_dtype,
+                      int64_t B, int64_t S, int64_t K,
+                      int64_t* indices, int64_t indices_rs,
+                      uint8_t* mask, int64_t mask_rs, void* stream);
+
+/*
+ * Gather of the selected query rows, hspmn_v2_1.py:185-186:
+ *   dst[b,i,:] = src[b, idx[b,i], :]     (row_bytes bytes per row)
+ * src strides (bytes): src_sb per sequence, src_ss per position.
+ * dst strides (bytes): dst_sb, dst_sk. idx: int64, row stride idx_sb.
+ */
+HSPMN_API int hspmn_gather_rows(const void* src, int64_t src_sb, int64_t src_ss,
+                      const int64_t* idx, int64_t idx_sb,
+                      void* dst, int64_t dst_sb, int64_t dst_sk,
+                      int64_t B, int64_t S, int64_t K, int64_t row_bytes,
+                      void* stream);
+
+/*
+ * Scatter into a zeroed stream, hspmn_v2_1.py:195-196:
+ *   dst[b,s,:] = src[b,i,:] if idx[b,i] == s for some i, else 0
+ * in one pass over dst (no separate zero fill). idx rows must be strictly
+ * ascending, as the router writes them; violations set HSPMN_DEVERR_UNSORTED.
+ */
+HSPMN_API int hspmn_scatter_rows(const void* src, int64_t src_sb, int64_t src_sk,
+                       const int64_t* idx, int64_t idx_sb,
+                       void* dst, int64_t dst_sb, int64_t dst_ss,
+                       int64_t B, int64_t S, int64_t K, int64_t row_bytes,
+                       void* stream);
+
+/*
+ * Sparse-query dense-key causal attention, the kernel behind
+ * sparse_query_dense_key_attention (kernels_v2_1.py:141-180, compute at
+ * kernels_v2_1.py:11-139), with grouped K/V heads as the reference's Flex
+ * path defines them (hspmn_v2_1.py:212):
+ *   o[b,i,h,:] = sum_{n <= idx[b,i]} softmax_n(sm_scale * q[b,i,h,:].k[b,n,g,:]) v[b,n,g,:]
+ *   with g = h / (H / Hkv).
+ * q, o: [B,K,H,hd]; k, v: [B,S,Hkv,hd]; strides in elements, innermost 1,
+ * the others multiples of 16 bytes, bases 16-byte aligned.
+ * dtype: HSPMN_BF16 or HSPMN_F16 (all of q, k, v, o). hd: a multiple of 8
+ * up to 128 (computed on a 64- or 128-wide tile).
+ * H % Hkv == 0 and H / Hkv <= 128.
+ */
+HSPMN_API int hspmn_sqdk_fwd(const void* q, const int64_t* q_strides,
+                   const void* k, const int64_t* k_strides,
+                   const void* v, const int64_t* v_strides,
+                   const int64_t* idx, int64_t idx_sb, int64_t idx_sk,
+                   void* o, const int64_t* o_strides,
+                   int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
+                   int64_t hd, int dtype, float sm_scale, void* stream);
+
+/*
+ * Read (and optionally clear) the current device's HSPMN_DEVERR_* flag word.
+ * Synchronises `stream` first.
+ */
+HSPMN_API int hspmn_device_errors(unsigned* bits, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HSPMN_SM100_H_ */

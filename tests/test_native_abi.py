@@ -1,0 +1,90 @@
+"""The C-ABI library: it loads, exports exactly what include/*.h declares and
+rejects bad arguments on the host (no kernel launches; runs without a GPU)."""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from hspmn_b200 import _native as N
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        names |= set(re.findall(r"HSPMN_API\s+[\w\s\*]+?\b(hspmn_\w+)\s*\(", open(h).read()))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert {"hspmn_router_topk", "hspmn_gather_rows", "hspmn_scatter_rows", "hspmn_sqdk_fwd"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(N.EXPORTED) >= declared_symbols()
+
+
+def test_version_and_strerror():
+    lib = N.lib()
+    assert lib.hspmn_version() >= 100
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert N.strerror(code)
+    assert N.strerror(-99) == "unknown status"
+
+
+def _i64(*v):
+    return N.i64_array(v)
+
+
+def test_sqdk_validation_rejects_before_launch():
+    lib = N.lib()
+    st = [64 * 4 * 128, 4 * 128, 128, 1]
+    p = ctypes.c_void_p(4096)
+    args = dict(q=p, qs=_i64(*st), k=p, ks=_i64(*st), v=p, vs=_i64(*st), idx=p, isb=8, isk=1, o=p,
+                os_=_i64(*st), B=1, K=8, S=64, H=4, Hkv=4, hd=128, dt=2, scale=0.088)
+
+    def call(**over):
+        a = dict(args, **over)
+        return lib.hspmn_sqdk_fwd(a["q"], a["qs"], a["k"], a["ks"], a["v"], a["vs"], a["idx"], a["isb"],
+                                  a["isk"], a["o"], a["os_"], a["B"], a["K"], a["S"], a["H"], a["Hkv"],
+                                  a["hd"], a["dt"], ctypes.c_float(a["scale"]), None)
+
+    assert call(q=ctypes.c_void_p(0)) == -1          # null pointer
+    assert call(dt=0) == -2                           # float32 not a tensor-core dtype here
+    assert call(hd=136) == -4 and call(hd=20) == -4   # unsupported head_dim
+    assert call(Hkv=3) == -4                          # 4 % 3 != 0
+    assert call(scale=-1.0) == -1
+    assert call(qs=_i64(64 * 4 * 128, 4 * 128, 128, 2)) == -3  # innermost stride must be 1
+    assert call(ks=_i64(64 * 4 * 128, 4 * 128, 132, 1)) == -3  # 264-byte head stride
+    assert call(B=0) == 0 and call(K=0) == 0          # empty: nothing to do
+
+
+def test_router_and_rows_validation():
+    lib = N.lib()
+    p = ctypes.c_void_p(4096)
+    # k > S, k < 1, bad dtype
+    assert lib.hspmn_router_topk(p, 2, 16, None, 0, 2, 1, 16, 17, p, 17, None, 0, None) == -1
+    assert lib.hspmn_router_topk(p, 2, 16, None, 0, 2, 1, 16, 0, p, 1, None, 0, None) == -1
+    assert lib.hspmn_router_topk(p, 7, 16, None, 0, 2, 1, 16, 4, p, 4, None, 0, None) == -2
+    # gather: null source; odd row bytes cannot be moved
+    assert lib.hspmn_gather_rows(None, 0, 0, p, 4, p, 0, 0, 1, 8, 4, 16, None) == -1
+    assert lib.hspmn_gather_rows(p, 8 * 3, 3, p, 4, p, 4 * 3, 3, 1, 8, 4, 3, None) == -3
+    # scatter: K > S
+    assert lib.hspmn_scatter_rows(p, 0, 16, p, 9, p, 0, 16, 1, 8, 9, 16, None) == -1
+
+
+def test_ops_reject_cpu_tensors():
+    torch = pytest.importorskip("torch")
+    from hspmn_b200 import ops
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ops.router_topk(torch.zeros(1, 8), None, 2, torch.float32)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ops.gather_rows(torch.zeros(1, 8, 4), torch.zeros(1, 2, dtype=torch.int64))

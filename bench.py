@@ -91,8 +91,8 @@ def load_peaks():
 
 def profiled_traffic(kernel: str, workload: str):
     """DRAM bytes per launch from the committed ncu summary
-    (profiles/<kernel>__<workload>.txt, line ``dram_bytes_per_launch = N``)."""
-    path = os.path.join(REPO, "profiles", f"{kernel}__{workload}.txt")
+    (profiles/<kernel>__<workload>.md, line ``dram_bytes_per_launch = N``)."""
+    path = os.path.join(REPO, "profiles", f"{kernel}__{workload}.md")
     try:
         with open(path) as f:
             for line in f:

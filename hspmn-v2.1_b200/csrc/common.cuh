@@ -66,14 +66,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Suspend-time hint for mbarrier waits: a waiting thread sleeps (up to this
+// long) instead of spinning, so polling does not take issue slots from the
+// warps doing the math. It wakes as soon as the phase completes.
+constexpr uint32_t kWaitSuspendNs = 200000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -98,6 +103,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   *abort = 1u;
   raise_device_error(HSPMN_DEVERR_TIMEOUT);
   return false;
+}
+
+// Named barrier over `nthreads` threads (whole warps) that also ANDs a
+// predicate across them: every participant gets the same result.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -247,6 +267,56 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---------------------------------------------------------------------------
+// packed float pairs (sm_100 f32x2 arithmetic: one instruction, two lanes)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe, for x <= 2^22 (x is clamped below at -125,
+// where 2^x is below every bf16/f16 normal). x = j + f with j = rint(x) taken
+// from the low mantissa bits of x + 1.5*2^23, f in [-0.5, 0.5];
+// 2^f ~ c0 + f*(c1 + f*(c2 + f*c3)), a cubic fitted to minimise the maximum
+// relative error on [-0.5, 0.5] (7.5e-5), and 2^j is added to the exponent.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(xc, f2_pack(kMagic, kMagic));
+  const uint64_t j = f2_add(t, f2_pack(-kMagic, -kMagic));
+  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), xc);
+  uint64_t p = f2_fma(f, f2_pack(0.05517167f, 0.05517167f), f2_pack(0.24261113f, 0.24261113f));
+  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  const float r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  const float r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+  return f2_pack(r0, r1);
 }
 
 }  // namespace hspmn

@@ -19,7 +19,9 @@
 //   S  = Q K^T        tcgen05.mma SS, M=128 N=64 K=hd, S in TMEM (2 buffers)
 //   P  = exp2(S*c - m) softmax warps: one thread per row, TMEM -> registers,
 //                     causal mask on the diagonal blocks, P written back to
-//                     TMEM as bf16/f16 over the S buffer it came from
+//                     TMEM as bf16/f16 over the S buffer it came from; a
+//                     quarter of the exponentials of unmasked blocks run on
+//                     the FMA pipe (cubic) to unload the MUFU unit
 //   O += P V          tcgen05.mma TS, A = P from TMEM, B = V (MN-major smem)
 // O stays in TMEM for the whole tile; it is rescaled only when a row's
 // running maximum grows by more than 2^8 (lazy rescaling), which with
@@ -43,6 +45,7 @@ constexpr int kSqdkBN = 64;        // keys per block
 constexpr int kSqdkStages = 2;     // depth of the K ring and of the V ring
 constexpr int kSqdkThreads = 192;  // 6 warps
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kSqdkPairGroup = 8;  // (sequence, kv-head) pairs scheduled together
 
 template <int HD>
 struct SqdkLayout {
@@ -109,10 +112,15 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   const uint32_t sbase = (smem_u32(sqdk_smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // tile coordinates: all (b, g) pairs of the last query tile first
+  // tile coordinates: (sequence, kv-head) pairs in groups of kSqdkPairGroup so
+  // the K/V blocks a group streams stay in L2; inside a group the longest
+  // query tiles (highest t) start first
   const int BG = p.B * p.Hkv;
-  const int t = p.T - 1 - static_cast<int>(blockIdx.x) / BG;
-  const int bg = static_cast<int>(blockIdx.x) % BG;
+  const int grp = static_cast<int>(blockIdx.x) / (kSqdkPairGroup * p.T);
+  const int in_grp = static_cast<int>(blockIdx.x) - grp * kSqdkPairGroup * p.T;
+  const int npairs = min(kSqdkPairGroup, BG - grp * kSqdkPairGroup);
+  const int t = p.T - 1 - in_grp / npairs;
+  const int bg = grp * kSqdkPairGroup + in_grp % npairs;
   const int b = bg / p.Hkv, g = bg % p.Hkv;
 
   if (threadIdx.x == 0) {
@@ -272,13 +280,20 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         }
       }
       const int lim = pos - j * kSqdkBN;  // columns <= lim are visible to this row
-      if (lim < kSqdkBN - 1) {
+      // warp-uniform: does any row of this warp need the causal mask here?
+      const bool diag = __any_sync(0xFFFFFFFFu, lim < kSqdkBN - 1);
+      if (diag) {
 #pragma unroll
         for (int c = 0; c < kSqdkBN; ++c) sv[c] = (c <= lim) ? sv[c] : -INFINITY;
       }
-      float mx = sv[0];
+      // row maximum: four independent chains
+      float mq[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int c = 1; c < kSqdkBN; ++c) mx = fmaxf(mx, sv[c]);
+      for (int c = 4; c < kSqdkBN; c += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mq[u] = fmaxf(mq[u], sv[c + u]);
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       const float m_new = fmaxf(m_run, mx * c2);
       const bool grow = m_new > m_run + kRescaleLog2;
       const bool need_o = grow && (m_run != -INFINITY);
@@ -304,16 +319,46 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         m_run = m_new;
       }
       const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
+      // p = 2^(s*c2 - m): scale with packed FMAs; exp2 on MUFU, and on the FMA
+      // pipe (cubic) for one pair in four of the unmasked blocks, so MUFU is
+      // not the only unit the softmax waits on; row sum with packed adds
+      const uint64_t cc = f2_pack(c2, c2), nm = f2_pack(neg_m, neg_m);
+      uint64_t acc0 = f2_pack(0.0f, 0.0f), acc1 = acc0;
       uint32_t pk[kSqdkBN / 2];
-      float lsum = 0.0f;
+      if (diag) {
 #pragma unroll
-      for (int c = 0; c < kSqdkBN; c += 2) {
-        const float p0 = fast_exp2(fmaf(sv[c], c2, neg_m));
-        const float p1 = fast_exp2(fmaf(sv[c + 1], c2, neg_m));
-        lsum += p0 + p1;
-        pk[c >> 1] = pack2<kBF16>(p0, p1);
+        for (int c = 0; c < kSqdkBN; c += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(sv[c], sv[c + 1]), cc, nm), x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          if ((c >> 1) & 1) acc1 = f2_add(acc1, f2_pack(p0, p1));
+          else acc0 = f2_add(acc0, f2_pack(p0, p1));
+          pk[c >> 1] = pack2<kBF16>(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kSqdkBN; c += 2) {
+          const uint64_t x = f2_fma(f2_pack(sv[c], sv[c + 1]), cc, nm);
+          float p0, p1;
+          if (((c >> 1) & 3) == 3) {
+            f2_unpack(f2_exp2_poly(x), p0, p1);
+          } else {
+            float x0, x1;
+            f2_unpack(x, x0, x1);
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          if ((c >> 1) & 1) acc1 = f2_add(acc1, f2_pack(p0, p1));
+          else acc0 = f2_add(acc0, f2_pack(p0, p1));
+          pk[c >> 1] = pack2<kBF16>(p0, p1);
+        }
       }
-      l_run += lsum;
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(acc0, a0, a1);
+        f2_unpack(acc1, b0, b1);
+        l_run += (a0 + a1) + (b0 + b1);
+      }
       tmem_st32(tS + sb * kSqdkBN, pk);
       tmem_wait_st();
       tc_fence_before();

@@ -20,7 +20,8 @@ numpy oracle port of HSPMNBlock.forward) on the host cores, one sequence of
 the same workload per step; under torchrun only rank 0 runs it.
 ``--workload sqdk-sweep`` runs the standalone router / gather / SQDK / scatter
 sweep (B=8, S=32768, H=Hkv=16, hd=128, k in {0.05, 0.1, 0.2, 0.5}) and
-prints one line per k.
+prints one line per k; ``--workload sqdk`` runs the same standalone path at
+``--batch/--seq-len/--heads/--kv-heads/--sparsity``.
 """
 
 from __future__ import annotations
@@ -52,7 +53,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "sqdk-sweep"], default="block")
+    ap.add_argument("--workload", choices=["block", "sqdk-sweep", "sqdk"], default="block")
     ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--dim", type=int, default=2048)
@@ -398,21 +399,21 @@ def run_block(args):
 # ---------------------------------------------------------------------------
 
 
-def run_sweep(args):
+def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
     import torch
 
     from hspmn_b200 import ops
 
     rank, world, local_rank = dist_env()
     dev = init_dist(world, local_rank)
-    B, S, H, hd = 8, 32768, 16, 128
+    hd = 128
     peaks, peak_src = load_peaks()
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     q = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
-    k = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
-    v = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
     logits = torch.randn(B, S, device=dev, dtype=torch.float32, generator=g)
-    for frac in (0.05, 0.1, 0.2, 0.5):
+    for frac in fracs:
         K = max(1, int(S * frac))
 
         def step():
@@ -437,11 +438,11 @@ def run_sweep(args):
         res = {n: r["ms"] / r["launches"] for n, r in kt.results().items()}
         if rank == 0:
             tf = flops / (res["sqdk_fwd"] / 1e3) / 1e12
-            gather_b = 2 * B * K * H * hd * 2 + B * K * 8
+            gather_b = 2 * B * K * H * hd * 2 + B * K * 8  # noqa: E501 (rows are H*hd wide)
             scatter_b = B * K * H * hd * 2 + B * S * H * hd * 2 + B * K * 8
             print(json.dumps({
-                "metric": "standalone SQDK sweep: attention TFLOP/s and gather/scatter GB/s", "workload":
-                f"B={B} S={S} H=Hkv={H} hd={hd} k={frac} (K={K}), router on f32 logits", "n_gpus": world,
+                "metric": "standalone SQDK: attention TFLOP/s and gather/scatter GB/s", "workload":
+                f"B={B} S={S} H={H} Hkv={Hkv} hd={hd} k={frac} (K={K}), router on f32 logits", "n_gpus": world,
                 "value": tf, "unit": "TFLOP/s", "frac_of_peak": tf / float(peaks["bf16_tflops"]),
                 "peak_source": f"{peak_src} bf16 dense, burst", "ms_per_step": ms / args.steps,
                 "router_us": res["router_topk"] * 1e3,
@@ -465,6 +466,8 @@ def main():
         raise SystemExit("--gpus N>1 needs torchrun: python -m torch.distributed.run --nproc-per-node N bench.py ...")
     if args.workload == "sqdk-sweep":
         return run_sweep(args)
+    if args.workload == "sqdk":
+        return run_sweep(args, args.batch, args.seq_len, args.heads, args.kv_heads, (args.sparsity,))
     return run_block(args)
 
 

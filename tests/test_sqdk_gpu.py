@@ -143,3 +143,16 @@ def test_padded_head_dims(hd):
     q, k, v, idx = make_case(2, 200, 4, 2, hd, 50, torch.bfloat16, seed=hd)
     o, ref = run_case(q, k, v, idx)
     check(o, ref, f"hd={hd}")
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd,K", [(4, 4096, 16, 4, 128, 820), (6, 2048, 8, 8, 64, 1024),
+                                            (5, 3000, 12, 4, 128, 640)])
+def test_persistent_many_tiles_per_cta(B, S, H, Hkv, hd, K):
+    """More 128-row tiles than the persistent grid has CTAs (2 per SM), so
+    each CTA runs several tiles back to back through the same pipeline."""
+    q, k, v, idx = make_case(B, S, H, Hkv, hd, K, torch.bfloat16, seed=B * S + K)
+    tiles = B * Hkv * -(-K // (128 // (H // Hkv)))
+    assert tiles > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    o, ref = run_case(q, k, v, idx)
+    check(o, ref, f"B={B} S={S} H={H} Hkv={Hkv} hd={hd} K={K}")
+    assert ops.device_errors() == 0

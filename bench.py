@@ -21,7 +21,9 @@ the same workload per step; under torchrun only rank 0 runs it.
 ``--workload sqdk-sweep`` runs the standalone router / gather / SQDK / scatter
 sweep (B=8, S=32768, H=Hkv=16, hd=128, k in {0.05, 0.1, 0.2, 0.5}) and
 prints one line per k; ``--workload sqdk`` runs the same standalone path at
-``--batch/--seq-len/--heads/--kv-heads/--sparsity``.
+``--batch/--seq-len/--heads/--kv-heads/--sparsity``. ``--workload long`` runs
+one sequence of ``--seq-len`` tokens (262144 for the long-context
+configuration) sequence-sharded over the ranks (strong scaling).
 """
 
 from __future__ import annotations
@@ -53,7 +55,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "sqdk-sweep", "sqdk"], default="block")
+    ap.add_argument("--workload", choices=["block", "sqdk-sweep", "sqdk", "long"], default="block")
     ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--dim", type=int, default=2048)
@@ -454,6 +456,72 @@ def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# long context: one sequence, sequence-sharded over the ranks
+# ---------------------------------------------------------------------------
+
+
+def run_long(args):
+    import torch
+
+    from hspmn_b200 import HSPMNBlock, HSPMNConfig, ops, seed_everything
+    from hspmn_b200.parallel import SequenceShardedBlock, ZigZagPlan
+
+    rank, world, local_rank = dist_env()
+    if world == 1:
+        # a one-rank process group keeps the code path identical to N > 1
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29531")
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+        dev = torch.device("cuda", local_rank)
+    else:
+        dev = init_dist(world, local_rank)
+    S = args.seq_len
+    seed_everything(42)
+    cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads, sparsity_k=args.sparsity,
+                      max_seq_len=S)
+    model = HSPMNBlock(cfg).to(dev, dtype=torch.bfloat16).eval()
+    plan = ZigZagPlan(S, world)
+    sb = SequenceShardedBlock(model, plan)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x_local = torch.randn(1, 2 * plan.chunk, args.dim, device=dev, dtype=torch.bfloat16, generator=g)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            sb.forward(x_local)
+        barrier(world)
+        launches0 = ops.LaunchStats.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ops.KernelTimer() as kt:
+            e0.record()
+            for _ in range(args.steps):
+                sb.forward(x_local)
+            e1.record()
+        torch.cuda.synchronize()
+        launches = ops.LaunchStats.launches - launches0
+        ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+        kres = kt.results()
+        sq = kres.get("sqdk_fwd", {"launches": 1, "ms": float("nan")})
+        sq_ms = max_over_ranks(sq["ms"] / max(1, sq["launches"]), world, dev)
+    import torch.distributed as dist
+    dist.destroy_process_group()
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        value = S * args.steps / (ms / 1e3)
+        print(json.dumps({
+            "metric": "long-context HSPMNBlock tok/s (one sequence, sequence-sharded)", "value": value,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
+            "config": {"workload": f"HSPMNBlock eval forward, B=1 S={S} dim={args.dim} heads={args.heads} "
+                                   f"kv_heads={args.kv_heads} k={args.sparsity}, zig-zag sequence shards",
+                       "seq_len": S, "parallelism": f"sequence-sharded x{world}, all-gather of logits and K/V"},
+            "sqdk_ms_per_launch_max_rank": sq_ms, "gpu_launches": launches,
+            "peak_source": peak_src}), flush=True)
+
+
 def main():
     args = parse_args()
     _, world, _ = dist_env()
@@ -466,6 +534,8 @@ def main():
         raise SystemExit("--gpus N>1 needs torchrun: python -m torch.distributed.run --nproc-per-node N bench.py ...")
     if args.workload == "sqdk-sweep":
         return run_sweep(args)
+    if args.workload == "long":
+        return run_long(args)
     if args.workload == "sqdk":
         return run_sweep(args, args.batch, args.seq_len, args.heads, args.kv_heads, (args.sparsity,))
     return run_block(args)

@@ -1,0 +1,227 @@
+"""Multi-GPU execution of the contextual-stream inference path.
+
+Two layouts, one process per GPU (``torch.distributed``, NCCL on GPUs):
+
+* Batch partitioning (independent sequences): every rank runs its own
+  sequences through an unmodified ``HSPMNBlock``; no collective touches the
+  data path. ``batch_slice`` gives a rank's share of a global batch.
+
+* Sequence sharding for one long sequence (the 262,144-token configuration):
+  the sequence is cut into ``2W`` equal chunks and rank ``r`` owns chunks ``r``
+  and ``2W-1-r`` ("zig-zag"), which balances the causal attention work. Per
+  forward there is one real exchange step:
+
+    1. every rank computes gate logits for its rows; an all-gather of the
+       logits (2 bytes per position) lets every rank run the same
+       deterministic top-K kernel, so the selected positions are identical
+       everywhere;
+    2. every rank computes K/V (with RoPE) for its rows; one all-gather brings
+       the whole K/V prefix into local HBM (no peer-memory loads);
+    3. each rank attends the selected queries that fall in its own chunks,
+       scatters them into its rows, applies o_proj and the reflexive stream
+       (the depthwise conv needs one neighbouring row per chunk edge, taken
+       from an all-gather of chunk-edge rows).
+
+  The output stays sequence-sharded in the rank's local row order.
+
+The compute operators are looked up on ``self.ops`` (default:
+``hspmn_b200.ops``, the CUDA kernels). The reference has no distributed code;
+this module follows its single-GPU semantics (hspmn_v2_1.py:95-238) exactly.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import ops as cuda_ops
+from .model import HSPMNBlock, RouterOutput, apply_rotary_pos_emb
+
+
+def batch_slice(global_batch: int, rank: int, world: int) -> slice:
+    """Contiguous share of a global batch for ``rank`` (sizes differ by <= 1)."""
+    base, extra = divmod(global_batch, world)
+    start = rank * base + min(rank, extra)
+    return slice(start, start + base + (1 if rank < extra else 0))
+
+
+@dataclass(frozen=True)
+class ZigZagPlan:
+    """Zig-zag split of ``seq_len`` positions over ``world`` ranks."""
+
+    seq_len: int
+    world: int
+
+    def __post_init__(self):
+        if self.seq_len % (2 * self.world) != 0:
+            raise ValueError(f"seq_len {self.seq_len} must be a multiple of 2*world ({2 * self.world})")
+
+    @property
+    def chunk(self) -> int:
+        return self.seq_len // (2 * self.world)
+
+    def chunks(self, rank: int) -> List[Tuple[int, int]]:
+        """[start, end) position ranges owned by ``rank``, ascending."""
+        c = self.chunk
+        a, b = rank, 2 * self.world - 1 - rank
+        return [(a * c, (a + 1) * c), (b * c, (b + 1) * c)]
+
+    def local_positions(self, rank: int, device=None) -> torch.Tensor:
+        """Global position of each local row (int64 [2*chunk], ascending)."""
+        return torch.cat([torch.arange(s, e, device=device) for s, e in self.chunks(rank)])
+
+    def shard(self, x: torch.Tensor, rank: int, dim: int = 1) -> torch.Tensor:
+        """This rank's rows of a full-sequence tensor (position dim ``dim``)."""
+        return torch.cat([x.narrow(dim, s, e - s) for s, e in self.chunks(rank)], dim=dim)
+
+    def unshard(self, parts: List[torch.Tensor], dim: int = 1) -> torch.Tensor:
+        """Inverse of ``shard`` given every rank's local tensor (rank order)."""
+        c = self.chunk
+        pieces = [None] * (2 * self.world)
+        for r, part in enumerate(parts):
+            a, b = r, 2 * self.world - 1 - r
+            pieces[a] = part.narrow(dim, 0, c)
+            pieces[b] = part.narrow(dim, c, c)
+        return torch.cat(pieces, dim=dim)
+
+
+def _all_gather_rows(local: torch.Tensor, plan: ZigZagPlan, group) -> torch.Tensor:
+    """All-gather a [B, 2*chunk, ...] local tensor into the full [B, S, ...]
+    sequence in position order (one collective, then one reorder copy)."""
+    W = plan.world
+    B = local.shape[0]
+    flat = torch.empty((W * B,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(flat, local.contiguous(), group=group)
+    return plan.unshard(list(flat.view((W, B) + tuple(local.shape[1:])).unbind(0)), dim=1)
+
+
+class SequenceShardedBlock:
+    """Inference forward of an ``HSPMNBlock`` over one sequence-sharded input.
+
+    ``forward(x_local)`` takes this rank's rows (``plan.shard(x, rank)``,
+    [B, 2*chunk, D]) and returns this rank's output rows and the auxiliary
+    loss, which every rank computes identically from the gathered logits."""
+
+    def __init__(self, block: HSPMNBlock, plan: ZigZagPlan, group=None, ops=None):
+        self.block = block
+        self.plan = plan
+        self.group = group
+        self.ops = ops if ops is not None else cuda_ops
+        self.rank = dist.get_rank(group)
+        if dist.get_world_size(group) != plan.world:
+            raise ValueError("plan.world does not match the process group size")
+
+    # -- router over the gathered logits (hspmn_v2_1.py:95-122, eval) ------
+    def _route(self, x_local: torch.Tensor, S: int) -> RouterOutput:
+        r = self.block.router
+        logits_local = r.gate(x_local).squeeze(-1)
+        logits = _all_gather_rows(logits_local, self.plan, self.group)
+        temp = torch.exp(r.log_temp).clamp(0.1, 2.0)
+        k = r.num_selected(S)
+        noisy_dtype = torch.result_type(logits, temp)
+        indices, mask = self.ops.router_topk(logits, temp, k, noisy_dtype)
+        probs = torch.sigmoid(logits)
+        sparsity_loss = (probs.mean() - r.target_sparsity).pow(2)
+        ent = -(probs * (probs + 1e-10).log() + (1.0 - probs) * (1.0 - probs + 1e-10).log())
+        aux = r.sparsity_coef * sparsity_loss + r.entropy_coef * ent.mean()
+        return RouterOutput(mask, indices, logits, aux)
+
+    def _local_selection(self, indices: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Selected positions inside this rank's chunks (ascending, [B, K_r])
+        and their local row numbers. Requires B == 1 or equal counts per row."""
+        B = indices.shape[0]
+        pos_list, row_list = [], []
+        for b in range(B):
+            ib = indices[b]
+            ps, rs = [], []
+            off = 0
+            for s, e in self.plan.chunks(self.rank):
+                lo = int(torch.searchsorted(ib, torch.tensor(s, device=ib.device)))
+                hi = int(torch.searchsorted(ib, torch.tensor(e, device=ib.device)))
+                seg = ib[lo:hi]
+                ps.append(seg)
+                rs.append(seg - s + off)
+                off += e - s
+            pos_list.append(torch.cat(ps))
+            row_list.append(torch.cat(rs))
+        n = {p.numel() for p in pos_list}
+        if len(n) != 1:
+            raise ValueError("per-sequence selection counts differ across the batch on this rank; "
+                             "shard one sequence per call")
+        return torch.stack(pos_list), torch.stack(row_list)
+
+    def _halo_rows(self, h_local: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Rows just before / after each local chunk (zeros at sequence ends),
+        from an all-gather of every rank's chunk-edge rows. Returns
+        (before [B,2,D], after [B,2,D]) for the rank's two chunks."""
+        c = self.plan.chunk
+        W = self.plan.world
+        edges = torch.stack([h_local[:, 0], h_local[:, c - 1], h_local[:, c], h_local[:, 2 * c - 1]], dim=1)
+        allg = torch.empty((W * edges.shape[0],) + tuple(edges.shape[1:]), dtype=edges.dtype,
+                           device=edges.device)
+        dist.all_gather_into_tensor(allg, edges.contiguous(), group=self.group)
+        allg = allg.view((W,) + tuple(edges.shape))
+        # first/last row of every global chunk
+        first = [None] * (2 * W)
+        last = [None] * (2 * W)
+        for r in range(W):
+            a, b = r, 2 * W - 1 - r
+            first[a], last[a] = allg[r, :, 0], allg[r, :, 1]
+            first[b], last[b] = allg[r, :, 2], allg[r, :, 3]
+        zero = torch.zeros_like(h_local[:, 0])
+        before, after = [], []
+        for ci in (self.rank, 2 * W - 1 - self.rank):
+            before.append(last[ci - 1] if ci > 0 else zero)
+            after.append(first[ci + 1] if ci < 2 * W - 1 else zero)
+        return torch.stack(before, 1), torch.stack(after, 1)
+
+    def _reflexive(self, x_local: torch.Tensor) -> torch.Tensor:
+        """ReflexiveStream.forward (hspmn_v2_1.py:141-145) on sharded rows:
+        the depthwise conv of each chunk sees its true neighbours."""
+        rf = self.block.reflexive
+        h = rf.norm(x_local)
+        before, after = self._halo_rows(h)
+        c = self.plan.chunk
+        outs = []
+        for i in range(2):
+            seg = torch.cat([before[:, i:i + 1], h[:, i * c:(i + 1) * c], after[:, i:i + 1]], dim=1)
+            conv = F.conv1d(seg.transpose(1, 2), rf.conv.weight, None, padding=0, groups=rf.conv.groups)
+            outs.append(conv.transpose(1, 2))
+        hc = torch.cat(outs, dim=1)
+        return x_local + rf.down_proj(F.silu(rf.gate_proj(hc)) * rf.up_proj(hc))
+
+    @torch.no_grad()
+    def forward(self, x_local: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        blk = self.block
+        B, S_local, D = x_local.shape
+        S = self.plan.seq_len
+        if S_local != 2 * self.plan.chunk:
+            raise ValueError(f"x_local has {S_local} rows; this rank owns {2 * self.plan.chunk}")
+        ro = self._route(x_local, S)
+        H, Hkv, hd = blk.num_heads, blk.num_kv_heads, blk.head_dim
+        x_norm = blk.norm(x_local)
+        pos = self.plan.local_positions(self.rank, device=x_local.device)
+        cos, sin = blk.rope(x_local, S)
+        cos, sin = cos[:, :, pos, :], sin[:, :, pos, :]
+        q = blk.q_proj(x_norm).view(B, S_local, H, hd).transpose(1, 2)
+        k = blk.k_proj(x_norm).view(B, S_local, Hkv, hd).transpose(1, 2)
+        v = blk.v_proj(x_norm).view(B, S_local, Hkv, hd).transpose(1, 2)
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        q_t, k_t, v_t = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        # the K/V prefix of the whole sequence, in local HBM
+        k_full = _all_gather_rows(k_t.contiguous(), self.plan, self.group)
+        v_full = _all_gather_rows(v_t.contiguous(), self.plan, self.group)
+        sel_pos, sel_rows = self._local_selection(ro.indices)
+        if sel_pos.shape[1] > 0:
+            q_sel = self.ops.gather_rows(q_t, sel_rows)
+            attn = self.ops.sqdk_fwd(q_sel, k_full, v_full, sel_pos, 1.0 / math.sqrt(hd))
+            out = self.ops.scatter_rows(attn, sel_rows, S_local)
+        else:
+            out = torch.zeros_like(q_t)
+        y = self._reflexive(x_local) + blk.o_proj(out.reshape(B, S_local, D))
+        return y, ro.aux_loss

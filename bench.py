@@ -222,7 +222,7 @@ def run_reference(args):
         "steps": steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": tok_s / PUBLISHED_TOK_S, "dtype": "f32",
         "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
-        "config": workload_config(args, per_gpu_batch=1),
+        "config": workload_config(args),
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

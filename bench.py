@@ -4,10 +4,11 @@
 Default workload (one JSON line on rank 0): HSPMNBlock eval forward, bf16,
 dim=2048, num_heads=16, num_kv_heads=4 (the config default), k=0.2, S=4096,
 64 sequences per GPU, x ~ N(0,1), default-init weights (seed 42). A step is
-one block forward over the GPU's batch; the router top-K, gather, SQDK
-attention and scatter inside it are this library's sm_100a kernels, the
-projections / norms / RoPE / reflexive stream are stock PyTorch (as in the
-reference). Multi-GPU: one process per GPU (torchrun), every rank runs its
+one block forward over the GPU's batch; the router top-K, the row gathers
+(with the query RoPE fused), SQDK attention and the residual write-back of
+the routed rows inside it are this library's sm_100a kernels; the
+projections (cuBLAS), norms, K RoPE and the reflexive stream are stock
+PyTorch. Multi-GPU: one process per GPU (torchrun), every rank runs its
 own 64 sequences with replicated weights and no data-path collective (weak
 scaling); the timed region is bracketed by barriers and the max over ranks is
 reported.
@@ -363,6 +364,12 @@ def run_block(args):
     if "gather_rows" in kernels:
         gb = 2 * B * k_sel * D * esz + B * k_sel * 8
         kernels["gather_rows"]["GB_s"] = gb / (kernels["gather_rows"]["ms_per_launch"] / 1e3) / 1e9
+    if "rope_gather_rows" in kernels:
+        gb = 2 * B * k_sel * D * esz + 2 * B * k_sel * (D // args.heads) * esz + B * k_sel * 8
+        kernels["rope_gather_rows"]["GB_s"] = gb / (kernels["rope_gather_rows"]["ms_per_launch"] / 1e3) / 1e9
+    if "scatter_add_rows" in kernels:
+        gb = 3 * B * k_sel * D * esz + B * k_sel * 8
+        kernels["scatter_add_rows"]["GB_s"] = gb / (kernels["scatter_add_rows"]["ms_per_launch"] / 1e3) / 1e9
     if "scatter_rows" in kernels:
         gb = B * k_sel * D * esz + B * S * D * esz + B * k_sel * 8
         kernels["scatter_rows"]["GB_s"] = gb / (kernels["scatter_rows"]["ms_per_launch"] / 1e3) / 1e9

@@ -222,6 +222,65 @@ int hspmn_scatter_rows(const void* src, int64_t src_sb, int64_t src_sk, const in
   return launch_status();
 }
 
+int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t src_ss, int src_by_position, const int64_t* idx,
+                           int64_t idx_sb, const void* cos_tab, const void* sin_tab, int64_t tab_ss, void* dst,
+                           int64_t dst_sb, int64_t dst_sk, int64_t B, int64_t S, int64_t K, int64_t H, int64_t hd,
+                           int dtype, void* stream) {
+  if (!src || !idx || !cos_tab || !sin_tab || !dst || B < 0 || S < 1 || K < 0 || H < 1 || hd < 2)
+    return HSPMN_ERR_INVALID;
+  if (!valid_dtype(dtype)) return HSPMN_ERR_DTYPE;
+  if (idx_sb < K || src_sb < 0 || src_ss < 0 || dst_sb < 0 || dst_sk < 0 || tab_ss < hd) return HSPMN_ERR_INVALID;
+  if (B == 0 || K == 0) return HSPMN_OK;
+  if (B * K > 0x7FFFFFFFLL * kRowWarps || H * hd > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  const int64_t es = dtype == HSPMN_F32 ? 4 : 2;
+  const int64_t vec = 16 / es;
+  if (hd % (2 * vec) != 0) return HSPMN_ERR_UNSUPPORTED;
+  if (!aligned(src, 16) || !aligned(dst, 16) || !aligned(cos_tab, 16) || !aligned(sin_tab, 16) ||
+      (src_sb * es) % 16 || (src_ss * es) % 16 || (dst_sb * es) % 16 || (dst_sk * es) % 16 || (tab_ss * es) % 16)
+    return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t blocks = (B * K + kRowWarps - 1) / kRowWarps;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  const unsigned g = static_cast<unsigned>(blocks);
+#define HSPMN_ROPE_LAUNCH(T)                                                                                       \
+  rope_gather_rows_kernel<T><<<g, kRowThreads, 0, st>>>(                                                          \
+      static_cast<const T*>(src), src_sb, src_ss, src_by_position, idx, idx_sb, static_cast<const T*>(cos_tab),     \
+      static_cast<const T*>(sin_tab), tab_ss, static_cast<T*>(dst), dst_sb, dst_sk, B, S, K, static_cast<int>(H),   \
+      static_cast<int>(hd))
+  if (dtype == HSPMN_BF16) HSPMN_ROPE_LAUNCH(__nv_bfloat16);
+  else if (dtype == HSPMN_F16) HSPMN_ROPE_LAUNCH(__half);
+  else HSPMN_ROPE_LAUNCH(float);
+#undef HSPMN_ROPE_LAUNCH
+  return launch_status();
+}
+
+int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t src_sk, const int64_t* idx, int64_t idx_sb,
+                           void* dst, int64_t dst_sb, int64_t dst_ss, int64_t B, int64_t S, int64_t K,
+                           int64_t row_elems, int dtype, void* stream) {
+  if (!src || !idx || !dst || B < 0 || S < 1 || K < 0 || row_elems < 1) return HSPMN_ERR_INVALID;
+  if (!valid_dtype(dtype)) return HSPMN_ERR_DTYPE;
+  if (idx_sb < K || src_sb < 0 || src_sk < 0 || dst_sb < 0 || dst_ss < 0) return HSPMN_ERR_INVALID;
+  if (B == 0 || K == 0) return HSPMN_OK;
+  const int64_t es = dtype == HSPMN_F32 ? 4 : 2;
+  if ((row_elems * es) % 16 || !aligned(src, 16) || !aligned(dst, 16) || (src_sb * es) % 16 || (src_sk * es) % 16 ||
+      (dst_sb * es) % 16 || (dst_ss * es) % 16)
+    return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t blocks = (B * K + kRowWarps - 1) / kRowWarps;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  const unsigned g = static_cast<unsigned>(blocks);
+#define HSPMN_SCATTER_ADD_LAUNCH(T)                                                                              \
+  scatter_add_rows_kernel<T><<<g, kRowThreads, 0, st>>>(static_cast<const T*>(src), src_sb, src_sk, idx, idx_sb, \
+                                                        static_cast<T*>(dst), dst_sb, dst_ss, B, S, K, row_elems)
+  if (dtype == HSPMN_BF16) HSPMN_SCATTER_ADD_LAUNCH(__nv_bfloat16);
+  else if (dtype == HSPMN_F16) HSPMN_SCATTER_ADD_LAUNCH(__half);
+  else HSPMN_SCATTER_ADD_LAUNCH(float);
+#undef HSPMN_SCATTER_ADD_LAUNCH
+  return launch_status();
+}
+
 int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
                    const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
                    const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,

@@ -100,3 +100,129 @@ __global__ void __launch_bounds__(kRowThreads) scatter_rows_kernel(
 }
 
 }  // namespace hspmn
+
+namespace hspmn {
+
+// ---------------------------------------------------------------------------
+// Rotary embedding fused into the gather of the selected rows.
+//
+// out[b,i,h,:] = rope(src row r, position idx[b,i]) with r = idx[b,i] when the
+// source holds all S positions, or r = i when it already holds the selected
+// rows. rope is apply_rotary_pos_emb (hspmn_v2_1.py:34-38,66-68) evaluated
+// with the reference's per-operation rounding in the element type T:
+//   t1 = T(x[d] * cos[p,d]);  t2 = T(rot[d] * sin[p,d]);  out = T(t1 + t2)
+// with rot = cat(-x[hd/2:], x[:hd/2]); products and the sum are single fp32
+// operations (products of two 16-bit values are exact in fp32), so the result
+// is bit-identical to running the three PyTorch ops on the full tensor.
+// ---------------------------------------------------------------------------
+
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  __device__ static float f(float v) { return v; }
+  __device__ static float r(float v) { return v; }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  __device__ static float f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ static __nv_bfloat16 r(float v) { return __float2bfloat16_rn(v); }
+};
+template <>
+struct Elem<__half> {
+  __device__ static float f(__half v) { return __half2float(v); }
+  __device__ static __half r(float v) { return __float2half_rn(v); }
+};
+
+template <typename T>
+__device__ __forceinline__ T rope_elem(T x, T partner, bool low_half, T c, T s) {
+  const float xf = Elem<T>::f(x);
+  const float rot = low_half ? -Elem<T>::f(partner) : Elem<T>::f(partner);
+  const T t1 = Elem<T>::r(__fmul_rn(xf, Elem<T>::f(c)));
+  const T t2 = Elem<T>::r(__fmul_rn(rot, Elem<T>::f(s)));
+  return Elem<T>::r(__fadd_rn(Elem<T>::f(t1), Elem<T>::f(t2)));
+}
+
+// One warp per selected row; each lane handles groups of 16 bytes (V
+// elements of T) of the output row of H*hd elements. hd is a multiple of
+// 2*V so a group never straddles the two halves of a head.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) rope_gather_rows_kernel(
+    const T* __restrict__ src, int64_t src_sb, int64_t src_ss, int src_by_position, const int64_t* __restrict__ idx,
+    int64_t idx_sb, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int64_t tab_ss, T* __restrict__ dst,
+    int64_t dst_sb, int64_t dst_sk, int64_t B, int64_t S, int64_t K, int H, int hd) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int row_elems = H * hd;
+  const int nvec = row_elems / V;
+  const int half = hd / 2;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5); r < B * K;
+       r += static_cast<int64_t>(gridDim.x) * kRowWarps) {
+    const int64_t b = r / K, i = r - b * K;
+    const int64_t pos = __ldg(idx + b * idx_sb + i);
+    T* d = dst + b * dst_sb + i * dst_sk;
+    if (pos < 0 || pos >= S) {
+      if (lane == 0) raise_device_error(HSPMN_DEVERR_POSITION);
+      for (int v = lane; v < nvec; v += 32) reinterpret_cast<uint4*>(d)[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const T* s = src + b * src_sb + (src_by_position ? pos : i) * src_ss;
+    const T* cr = cos_t + pos * tab_ss;
+    const T* sr = sin_t + pos * tab_ss;
+    for (int v = lane; v < nvec; v += 32) {
+      const int e = v * V;
+      const int h = e / hd, dd = e - h * hd;
+      const bool low = dd < half;
+      const int pe = h * hd + (low ? dd + half : dd - half);
+      const uint4 xv = __ldg(reinterpret_cast<const uint4*>(s + e));
+      const uint4 pv = __ldg(reinterpret_cast<const uint4*>(s + pe));
+      const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cr + dd));
+      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sr + dd));
+      const T* xa = reinterpret_cast<const T*>(&xv);
+      const T* pa = reinterpret_cast<const T*>(&pv);
+      const T* ca = reinterpret_cast<const T*>(&cv);
+      const T* sa = reinterpret_cast<const T*>(&sv);
+      uint4 ov;
+      T* oa = reinterpret_cast<T*>(&ov);
+#pragma unroll
+      for (int u = 0; u < V; ++u) oa[u] = rope_elem<T>(xa[u], pa[u], low, ca[u], sa[u]);
+      reinterpret_cast<uint4*>(d)[v] = ov;
+    }
+  }
+}
+
+// dst[b, idx[b,i], :] = T(dst[b, idx[b,i], :] + src[b,i,:]) — the residual
+// add of hspmn_v2_1.py:238 restricted to the rows the attention wrote (every
+// other row of o_proj(scatter(...)) is zero). One warp per selected row.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) scatter_add_rows_kernel(
+    const T* __restrict__ src, int64_t src_sb, int64_t src_sk, const int64_t* __restrict__ idx, int64_t idx_sb,
+    T* __restrict__ dst, int64_t dst_sb, int64_t dst_ss, int64_t B, int64_t S, int64_t K, int64_t row_elems) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t nvec = row_elems / V;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5); r < B * K;
+       r += static_cast<int64_t>(gridDim.x) * kRowWarps) {
+    const int64_t b = r / K, i = r - b * K;
+    const int64_t pos = __ldg(idx + b * idx_sb + i);
+    if (pos < 0 || pos >= S) {
+      if (lane == 0) raise_device_error(HSPMN_DEVERR_POSITION);
+      continue;
+    }
+    const uint4* sv = reinterpret_cast<const uint4*>(src + b * src_sb + i * src_sk);
+    uint4* dv = reinterpret_cast<uint4*>(dst + b * dst_sb + pos * dst_ss);
+    for (int64_t v = lane; v < nvec; v += 32) {
+      const uint4 a = __ldcs(sv + v);
+      const uint4 o = dv[v];
+      const T* aa = reinterpret_cast<const T*>(&a);
+      const T* oa = reinterpret_cast<const T*>(&o);
+      uint4 w;
+      T* wa = reinterpret_cast<T*>(&w);
+#pragma unroll
+      for (int u = 0; u < V; ++u) wa[u] = Elem<T>::r(__fadd_rn(Elem<T>::f(oa[u]), Elem<T>::f(aa[u])));
+      dv[v] = w;
+    }
+  }
+}
+
+}  // namespace hspmn

@@ -29,6 +29,10 @@ _SIGNATURES = {
     "hspmn_scatter_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "hspmn_sqdk_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp,
                               _i64, _i64, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _vp]),
+    "hspmn_rope_gather_rows": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64,
+                                      _i64, _i64, _i64, _i64, _i64, _int, _vp]),
+    "hspmn_scatter_add_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                      _int, _vp]),
     "hspmn_device_errors": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _vp]),
 }
 EXPORTED = tuple(_SIGNATURES)

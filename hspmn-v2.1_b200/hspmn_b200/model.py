@@ -3,8 +3,12 @@
 Parameter names, buffers, init and forward semantics follow the reference
 (hspmn_v2_1.py:26-238) so ``state_dict``s load across. In eval mode the
 contextual stream runs the B200 path: router selection (``ops.router_topk``),
-gather (``ops.gather_rows``), SQDK attention (``ops.sqdk_fwd``) and the
-zero-filling scatter (``ops.scatter_rows``), all sm_100a CUDA kernels. The
+gather, SQDK attention (``ops.sqdk_fwd``) and the write-back, all sm_100a CUDA
+kernels. By default (``sqdk_fused``) the write-back skips the zero-filled
+scatter: q_proj, RoPE and o_proj run only on the routed rows and the result
+is added into the residual in place (``ops.scatter_add_rows_``); with
+``sqdk_fused = False`` the reference's order (gather -> SQDK -> zero-filling
+``ops.scatter_rows`` -> o_proj on all rows) is used. The
 surrounding projections, norms, RoPE and the reflexive stream are stock
 PyTorch, as in the reference. Training mode keeps the reference's
 FlexAttention formulation (hspmn_v2_1.py:200-216), which is outside the
@@ -192,6 +196,9 @@ class HSPMNBlock(nn.Module):
         self.o_proj = nn.Linear(config.dim, config.dim, bias=False)
         self.rope = RotaryEmbedding(self.head_dim, config.max_seq_len, config.rope_base)
         self.reflexive = ReflexiveStream(config.dim, config.mlp_ratio)
+        # eval: run q_proj / RoPE / o_proj only on the routed rows (True), or
+        # follow the reference's operation order on all rows (False)
+        self.sqdk_fused = True
         self._init_weights()
 
     def _init_weights(self):
@@ -212,6 +219,30 @@ class HSPMNBlock(nn.Module):
         attn = ops.sqdk_fwd(q_sel, k_t, v_t, idx, 1.0 / math.sqrt(self.head_dim))
         out = ops.scatter_rows(attn, idx, S)
         return self.o_proj(out.view(B, S, D))
+
+    def _attention_sqdk_fused(self, x_norm: torch.Tensor, idx: torch.Tensor, B: int, S: int,
+                              D: int) -> torch.Tensor:
+        """The same contextual stream with the work outside SQDK cut to the
+        selected rows: q_proj on the gathered rows only, RoPE fused into their
+        gather (bit-identical rows), K/V projections + RoPE on all rows as in
+        the reference, and o_proj on the K attention rows only. Returns the
+        [B,K,D] rows of ``o_proj(scatter(attn))`` (every other row is zero);
+        the caller adds them into the residual at ``idx``."""
+        H, Hkv, hd = self.num_heads, self.num_kv_heads, self.head_dim
+        K = idx.shape[1]
+        x_sel = ops.gather_rows(x_norm, idx)
+        q_sel = self.q_proj(x_sel).view(B, K, H, hd)
+        cos, sin = self.rope(x_norm, S)
+        q_sel = ops.rope_gather_rows(q_sel, idx, cos, sin, False)
+        k = self.k_proj(x_norm).view(B, S, Hkv, hd).transpose(1, 2)
+        v = self.v_proj(x_norm).view(B, S, Hkv, hd).transpose(1, 2)
+        k = (k * cos) + (rotate_half(k) * sin)  # hspmn_v2_1.py:66-68 on K
+        attn = ops.sqdk_fwd(q_sel, k.transpose(1, 2), v.transpose(1, 2), idx, 1.0 / math.sqrt(hd))
+        return self.o_proj(attn.reshape(B, K, D))
+
+    def _fused_ok(self, x: torch.Tensor) -> bool:
+        vec = 16 // x.element_size()
+        return self.sqdk_fused and self.head_dim % (2 * vec) == 0
 
     # -- contextual stream, training: reference FlexAttention formulation --
     def _attention_flex(self, q, k, v, router_out: RouterOutput, B: int, S: int, D: int) -> torch.Tensor:
@@ -242,4 +273,10 @@ class HSPMNBlock(nn.Module):
 
     def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         router_out = self.router(x)
+        if not self.training and router_out.indices is not None and self._fused_ok(x):
+            B, S, D = x.shape
+            o_sel = self._attention_sqdk_fused(self.norm(x), router_out.indices, B, S, D)
+            y = self.reflexive(x).contiguous()
+            ops.scatter_add_rows_(y, router_out.indices, o_sel)
+            return y, router_out.aux_loss
         return self.reflexive(x) + self._attention(x, router_out), router_out.aux_loss

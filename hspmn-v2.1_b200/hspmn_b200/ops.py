@@ -253,6 +253,79 @@ def _(src, indices, seq_len):
     return src.new_empty((src.shape[0], seq_len) + tuple(src.shape[2:]))
 
 
+@torch.library.custom_op("hspmn::rope_gather_rows", mutates_args=())
+def rope_gather_rows(src: torch.Tensor, indices: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                     src_by_position: bool) -> torch.Tensor:
+    """Selected query rows with the rotary embedding applied, bit-identical to
+    ``gather(apply_rotary_pos_emb(q))`` (hspmn_v2_1.py:66-68,185-186).
+
+    ``src`` is [B,S,H,hd] (all positions; ``src_by_position=True``) or
+    [B,K,H,hd] (already the selected rows); ``cos``/``sin`` are the [S,hd]
+    (or [1,1,S,hd]) tables in ``src``'s dtype; ``indices`` int64 [B,K] give
+    the positions. Returns [B,K,H,hd]."""
+    dev = _require_cuda(src, indices, cos, sin)
+    if src.dim() != 4:
+        raise ValueError("rope_gather_rows: src must be [B,S|K,H,hd]")
+    B, _, H, hd = src.shape
+    K = indices.shape[1]
+    cos2, sin2 = cos.reshape(-1, hd), sin.reshape(-1, hd)
+    if cos2.dtype != src.dtype or sin2.dtype != src.dtype:
+        raise TypeError("rope_gather_rows: cos/sin must have src's dtype")
+    if cos2.stride(1) != 1 or sin2.stride(1) != 1 or cos2.stride(0) != sin2.stride(0):
+        cos2, sin2 = cos2.contiguous(), sin2.contiguous()
+    S = cos2.shape[0]
+    if indices.stride(1) != 1:
+        indices = indices.contiguous()
+    src, _ = _rows_view(src, 2)
+    out = torch.empty((B, K, H, hd), dtype=src.dtype, device=dev)
+    with _on_device(dev), _launch("rope_gather_rows", dev):
+        rc = N.lib().hspmn_rope_gather_rows(
+            ctypes.c_void_p(src.data_ptr()), src.stride(0), src.stride(1), int(src_by_position),
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0),
+            ctypes.c_void_p(cos2.data_ptr()), ctypes.c_void_p(sin2.data_ptr()), cos2.stride(0),
+            ctypes.c_void_p(out.data_ptr()), out.stride(0), out.stride(1), B, S, K, H, hd,
+            dtype_code(src.dtype), _stream(dev))
+        N.check(rc, "hspmn_rope_gather_rows")
+    return out
+
+
+@rope_gather_rows.register_fake
+def _(src, indices, cos, sin, src_by_position):
+    return src.new_empty((src.shape[0], indices.shape[1]) + tuple(src.shape[2:]))
+
+
+@torch.library.custom_op("hspmn::scatter_add_rows_", mutates_args=("dst",))
+def scatter_add_rows_(dst: torch.Tensor, indices: torch.Tensor, src: torch.Tensor) -> None:
+    """In place ``dst[b, indices[b,i]] += src[b,i]`` in ``dst``'s dtype (the
+    residual add of hspmn_v2_1.py:238 restricted to the selected rows).
+    ``dst`` [B,S,...] with dense rows, ``src`` [B,K,...]."""
+    dev = _require_cuda(dst, indices, src)
+    if src.dtype != dst.dtype:
+        raise TypeError("scatter_add_rows_: src and dst dtypes differ")
+    B, S = dst.shape[0], dst.shape[1]
+    K = indices.shape[1]
+    row = 1
+    for d in dst.shape[2:]:
+        row *= d
+    if not dst.is_contiguous():
+        raise ValueError("scatter_add_rows_: dst must be contiguous")
+    if indices.stride(1) != 1:
+        indices = indices.contiguous()
+    src = src.contiguous()
+    with _on_device(dev), _launch("scatter_add_rows", dev):
+        rc = N.lib().hspmn_scatter_add_rows(
+            ctypes.c_void_p(src.data_ptr()), src.stride(0), src.stride(1),
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0),
+            ctypes.c_void_p(dst.data_ptr()), dst.stride(0), dst.stride(1), B, S, K, row,
+            dtype_code(dst.dtype), _stream(dev))
+        N.check(rc, "hspmn_scatter_add_rows")
+
+
+@scatter_add_rows_.register_fake
+def _(dst, indices, src):
+    return None
+
+
 # ---------------------------------------------------------------------------
 # SQDK attention
 # ---------------------------------------------------------------------------

@@ -101,6 +101,39 @@ HSPMN_API int hspmn_scatter_rows(const void* src, int64_t src_sb, int64_t src_sk
                        void* stream);
 
 /*
+ * Rotary embedding of the selected query rows, fused with their gather
+ * (apply_rotary_pos_emb at hspmn_v2_1.py:66-68 on q, then hspmn_v2_1.py:185-186):
+ *   dst[b,i,h,:] = rope(src[b, r, h, :], idx[b,i]),  r = idx[b,i] if
+ *   src_by_position else i,
+ *   rope(x, p)[d] = T(T(x[d]*cos[p,d]) + T(rot(x)[d]*sin[p,d])),
+ *   rot(x) = cat(-x[hd/2:], x[:hd/2])
+ * with the same per-operation rounding as the reference's three tensor ops,
+ * so the rows are bit-identical to gathering after a full-tensor RoPE.
+ * src rows: H*hd elements (strides in elements). cos/sin: [S, hd] tables of
+ * the same dtype, row stride tab_ss. hd must be a multiple of 16 (bf16/f16)
+ * or 8 (f32); rows, strides and tables 16-byte aligned.
+ */
+HSPMN_API int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t src_ss,
+                                     int src_by_position, const int64_t* idx, int64_t idx_sb,
+                                     const void* cos_tab, const void* sin_tab, int64_t tab_ss,
+                                     void* dst, int64_t dst_sb, int64_t dst_sk,
+                                     int64_t B, int64_t S, int64_t K, int64_t H, int64_t hd,
+                                     int dtype, void* stream);
+
+/*
+ * In-place residual add of the selected rows (hspmn_v2_1.py:238 where every
+ * unselected row of o_proj(scatter(...)) is zero):
+ *   dst[b, idx[b,i], :] = T(dst[b, idx[b,i], :] + src[b,i,:])
+ * row_elems elements per row; strides in elements; rows 16-byte aligned.
+ * idx rows must not repeat a position (the router's never do).
+ */
+HSPMN_API int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t src_sk,
+                                     const int64_t* idx, int64_t idx_sb,
+                                     void* dst, int64_t dst_sb, int64_t dst_ss,
+                                     int64_t B, int64_t S, int64_t K, int64_t row_elems,
+                                     int dtype, void* stream);
+
+/*
  * Sparse-query dense-key causal attention, the kernel behind
  * sparse_query_dense_key_attention (kernels_v2_1.py:141-180, compute at
  * kernels_v2_1.py:11-139), with grouped K/V heads as the reference's Flex

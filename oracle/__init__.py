@@ -29,5 +29,6 @@ from .sqdk_oracle import (  # noqa: F401
     rms_norm,
     rope_tables,
     apply_rope,
+    rope_rounded,
     block_forward,
 )

@@ -217,6 +217,19 @@ def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
     return x * cos[None, :, None, :] + rot * sin[None, :, None, :]
 
 
+def rope_rounded(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, dtype: str) -> np.ndarray:
+    """``(x*cos) + (rotate_half(x)*sin)`` (hspmn_v2_1.py:34-38,66-68) evaluated
+    as the reference's three tensor ops in ``dtype``: each product and the sum
+    computed in float32 and rounded to ``dtype``. x [..., hd] with values of
+    ``dtype``; cos/sin broadcastable, already rounded to ``dtype``."""
+    x = np.asarray(x, dtype=F32)
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    t1 = round_to(x * np.asarray(cos, F32), dtype)
+    t2 = round_to(rot * np.asarray(sin, F32), dtype)
+    return round_to(t1 + t2, dtype)
+
+
 def _silu(x):
     return x / (F32(1.0) + np.exp(-x))
 

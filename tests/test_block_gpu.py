@@ -161,8 +161,9 @@ def test_block_bf16_cfg2_shape_against_oracle():
     err = np.abs(o.float().cpu().numpy() - ref_o)
     assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
     np.testing.assert_array_equal(out.float().cpu().numpy(), oracle.scatter_rows(o.float().cpu().numpy(), idx, S))
-    # and the full forward runs that same path
+    # the reference-order forward runs exactly that path
     with torch.no_grad():
+        block.sqdk_fused = False
         y, _ = block(x)
         y_ref = block.reflexive(x) + block.o_proj(out.view(B, S, D))
     assert torch.equal(y, y_ref)

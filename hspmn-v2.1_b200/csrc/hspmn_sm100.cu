@@ -229,7 +229,8 @@ int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t src_ss, int 
   if (!src || !idx || !cos_tab || !sin_tab || !dst || B < 0 || S < 1 || K < 0 || H < 1 || hd < 2)
     return HSPMN_ERR_INVALID;
   if (!valid_dtype(dtype)) return HSPMN_ERR_DTYPE;
-  if (idx_sb < K || src_sb < 0 || src_ss < 0 || dst_sb < 0 || dst_sk < 0 || tab_ss < hd) return HSPMN_ERR_INVALID;
+  // idx_sb may be 0: every sequence reads the same positions (e.g. all of them)
+  if (idx_sb < 0 || src_sb < 0 || src_ss < 0 || dst_sb < 0 || dst_sk < 0 || tab_ss < hd) return HSPMN_ERR_INVALID;
   if (B == 0 || K == 0) return HSPMN_OK;
   if (B * K > 0x7FFFFFFFLL * kRowWarps || H * hd > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
   const int64_t es = dtype == HSPMN_F32 ? 4 : 2;

@@ -234,10 +234,12 @@ class HSPMNBlock(nn.Module):
         q_sel = self.q_proj(x_sel).view(B, K, H, hd)
         cos, sin = self.rope(x_norm, S)
         q_sel = ops.rope_gather_rows(q_sel, idx, cos, sin, False)
-        k = self.k_proj(x_norm).view(B, S, Hkv, hd).transpose(1, 2)
-        v = self.v_proj(x_norm).view(B, S, Hkv, hd).transpose(1, 2)
-        k = (k * cos) + (rotate_half(k) * sin)  # hspmn_v2_1.py:66-68 on K
-        attn = ops.sqdk_fwd(q_sel, k.transpose(1, 2), v.transpose(1, 2), idx, 1.0 / math.sqrt(hd))
+        # K RoPE on every position in one pass (same rounding as the reference's
+        # three tensor ops, hspmn_v2_1.py:66-68)
+        positions = torch.arange(S, device=x_norm.device).expand(B, S)
+        k = ops.rope_gather_rows(self.k_proj(x_norm).view(B, S, Hkv, hd), positions, cos, sin, False)
+        v = self.v_proj(x_norm).view(B, S, Hkv, hd)
+        attn = ops.sqdk_fwd(q_sel, k, v, idx, 1.0 / math.sqrt(hd))
         return self.o_proj(attn.reshape(B, K, D))
 
     def _fused_ok(self, x: torch.Tensor) -> bool:

@@ -17,10 +17,11 @@ Two layouts, one process per GPU (``torch.distributed``, NCCL on GPUs):
        everywhere;
     2. every rank computes K/V (with RoPE) for its rows; one all-gather brings
        the whole K/V prefix into local HBM (no peer-memory loads);
-    3. each rank attends the selected queries that fall in its own chunks,
-       scatters them into its rows, applies o_proj and the reflexive stream
-       (the depthwise conv needs one neighbouring row per chunk edge, taken
-       from an all-gather of chunk-edge rows).
+    3. each rank attends the selected queries that fall in its own chunks
+       (q_proj on those rows only, RoPE fused into their gather), applies
+       o_proj to the attention rows and adds them into its rows of the
+       reflexive stream (whose depthwise conv needs one neighbouring row per
+       chunk edge, taken from an all-gather of chunk-edge rows).
 
   The output stays sequence-sharded in the rank's local row order.
 
@@ -40,7 +41,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import ops as cuda_ops
-from .model import HSPMNBlock, RouterOutput, apply_rotary_pos_emb
+from .model import HSPMNBlock, RouterOutput
 
 
 def batch_slice(global_batch: int, rank: int, world: int) -> slice:
@@ -205,23 +206,23 @@ class SequenceShardedBlock:
         ro = self._route(x_local, S)
         H, Hkv, hd = blk.num_heads, blk.num_kv_heads, blk.head_dim
         x_norm = blk.norm(x_local)
-        pos = self.plan.local_positions(self.rank, device=x_local.device)
         cos, sin = blk.rope(x_local, S)
-        cos, sin = cos[:, :, pos, :], sin[:, :, pos, :]
-        q = blk.q_proj(x_norm).view(B, S_local, H, hd).transpose(1, 2)
-        k = blk.k_proj(x_norm).view(B, S_local, Hkv, hd).transpose(1, 2)
-        v = blk.v_proj(x_norm).view(B, S_local, Hkv, hd).transpose(1, 2)
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
-        q_t, k_t, v_t = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-        # the K/V prefix of the whole sequence, in local HBM
-        k_full = _all_gather_rows(k_t.contiguous(), self.plan, self.group)
-        v_full = _all_gather_rows(v_t.contiguous(), self.plan, self.group)
+        pos = self.plan.local_positions(self.rank, device=x_local.device).expand(B, S_local)
+        # K (RoPE at the rows' global positions) and V of the local rows, then
+        # the whole sequence's K/V prefix into local HBM
+        k_loc = self.ops.rope_gather_rows(blk.k_proj(x_norm).view(B, S_local, Hkv, hd), pos, cos, sin, False)
+        v_loc = blk.v_proj(x_norm).view(B, S_local, Hkv, hd)
+        k_full = _all_gather_rows(k_loc.contiguous(), self.plan, self.group)
+        v_full = _all_gather_rows(v_loc.contiguous(), self.plan, self.group)
+        y = self._reflexive(x_local).contiguous()
         sel_pos, sel_rows = self._local_selection(ro.indices)
         if sel_pos.shape[1] > 0:
-            q_sel = self.ops.gather_rows(q_t, sel_rows)
+            # the routed queries of this rank: q_proj on those rows only, RoPE at
+            # their global positions fused into the gather, o_proj on the K
+            # attention rows, residual add in place
+            x_sel = self.ops.gather_rows(x_norm, sel_rows)
+            q_sel = blk.q_proj(x_sel).view(B, -1, H, hd)
+            q_sel = self.ops.rope_gather_rows(q_sel, sel_pos, cos, sin, False)
             attn = self.ops.sqdk_fwd(q_sel, k_full, v_full, sel_pos, 1.0 / math.sqrt(hd))
-            out = self.ops.scatter_rows(attn, sel_rows, S_local)
-        else:
-            out = torch.zeros_like(q_t)
-        y = self._reflexive(x_local) + blk.o_proj(out.reshape(B, S_local, D))
+            self.ops.scatter_add_rows_(y, sel_rows, blk.o_proj(attn.reshape(B, -1, D)))
         return y, ro.aux_loss

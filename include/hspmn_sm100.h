@@ -109,8 +109,9 @@ HSPMN_API int hspmn_scatter_rows(const void* src, int64_t src_sb, int64_t src_sk
  *   rot(x) = cat(-x[hd/2:], x[:hd/2])
  * with the same per-operation rounding as the reference's three tensor ops,
  * so the rows are bit-identical to gathering after a full-tensor RoPE.
- * src rows: H*hd elements (strides in elements). cos/sin: [S, hd] tables of
- * the same dtype, row stride tab_ss. hd must be a multiple of 16 (bf16/f16)
+ * src rows: H*hd elements (strides in elements). idx row stride idx_sb may be
+ * 0 (all sequences use one position list). cos/sin: [S, hd] tables of the
+ * same dtype, row stride tab_ss. hd must be a multiple of 16 (bf16/f16)
  * or 8 (f32); rows, strides and tables 16-byte aligned.
  */
 HSPMN_API int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t src_ss,

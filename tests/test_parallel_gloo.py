@@ -46,6 +46,21 @@ class OracleOps:
     def scatter_rows(src, idx, S):
         return torch.from_numpy(oracle.scatter_rows(src.float().numpy(), idx.numpy(), S)).to(src.dtype)
 
+    @staticmethod
+    def rope_gather_rows(src, idx, cos, sin, by_position):
+        hd = src.shape[-1]
+        c, s = cos.reshape(-1, hd).float().numpy(), sin.reshape(-1, hd).float().numpy()
+        rows = oracle.gather_rows(src.float().numpy(), idx.numpy()) if by_position else src.float().numpy()
+        ix = idx.numpy()
+        out = np.stack([oracle.rope_rounded(rows[b], c[ix[b]][:, None, :], s[ix[b]][:, None, :], "f32")
+                        for b in range(rows.shape[0])])
+        return torch.from_numpy(out).to(src.dtype)
+
+    @staticmethod
+    def scatter_add_rows_(dst, idx, src):
+        for b in range(dst.shape[0]):
+            dst[b, idx[b]] += src[b]
+
 
 def _free_port():
     with socket.socket() as s:

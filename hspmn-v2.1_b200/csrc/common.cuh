@@ -295,28 +295,5 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe, for x <= 2^22 (x is clamped below at -125,
-// where 2^x is below every bf16/f16 normal). x = j + f with j = rint(x) taken
-// from the low mantissa bits of x + 1.5*2^23, f in [-0.5, 0.5];
-// 2^f ~ c0 + f*(c1 + f*(c2 + f*c3)), a cubic fitted to minimise the maximum
-// relative error on [-0.5, 0.5] (7.5e-5), and 2^j is added to the exponent.
-__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  float x0, x1;
-  f2_unpack(x, x0, x1);
-  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t t = f2_add(xc, f2_pack(kMagic, kMagic));
-  const uint64_t j = f2_add(t, f2_pack(-kMagic, -kMagic));
-  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), xc);
-  uint64_t p = f2_fma(f, f2_pack(0.05517167f, 0.05517167f), f2_pack(0.24261113f, 0.24261113f));
-  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
-  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  const float r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-  const float r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-  return f2_pack(r0, r1);
-}
 
 }  // namespace hspmn

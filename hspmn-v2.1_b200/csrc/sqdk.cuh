@@ -19,13 +19,14 @@
 //   S  = Q K^T        tcgen05.mma SS, M=128 N=64 K=hd, S in TMEM (2 buffers)
 //   P  = exp2(S*c - m) softmax warps: one thread per row, TMEM -> registers,
 //                     causal mask on the diagonal blocks, P written back to
-//                     TMEM as bf16/f16 over the S buffer it came from; a
-//                     quarter of the exponentials of unmasked blocks run on
-//                     the FMA pipe (cubic) to unload the MUFU unit
+//                     TMEM as bf16/f16 over the S buffer it came from
 //   O += P V          tcgen05.mma TS, A = P from TMEM, B = V (MN-major smem)
-// O stays in TMEM for the whole tile; it is rescaled only when a row's
-// running maximum grows by more than 2^8 (lazy rescaling), which with
-// fp32 accumulation is exact up to rounding.
+// O stays in TMEM for the whole tile. A block is first exponentiated against
+// the row's running maximum m without computing the block's own maximum:
+// softmax is exact for any m as long as nothing overflows, and the block's
+// row sum (needed anyway) bounds every term. Only a row's first block, or a
+// block whose sum exceeds the bound (the maximum grew a lot), takes the exact
+// path: block maximum, O and l rescaled, P recomputed.
 //
 // Warp roles (192 threads, two CTAs per SM):
 //   warp 0      TMA producer: Q once, then K_j / V_j through 2-stage rings
@@ -44,7 +45,11 @@ constexpr int kSqdkBM = 128;       // rows per tile
 constexpr int kSqdkBN = 64;        // keys per block
 constexpr int kSqdkStages = 2;     // depth of the K ring and of the V ring
 constexpr int kSqdkThreads = 192;  // 6 warps
-constexpr float kRescaleLog2 = 8.0f;
+// Largest row sum of one block accepted without an exact row maximum: every
+// p of the row is below it, so P stays finite in bf16 (and below 65504 in
+// f16) and O = sum(P V) in fp32 cannot overflow.
+template <bool kBF16>
+constexpr float kSqdkSumBound = kBF16 ? 1048576.0f : 32768.0f;
 constexpr int kSqdkPairGroup = 8;  // (sequence, kv-head) pairs scheduled together
 
 template <int HD>
@@ -286,46 +291,13 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 #pragma unroll
         for (int c = 0; c < kSqdkBN; ++c) sv[c] = (c <= lim) ? sv[c] : -INFINITY;
       }
-      // row maximum: four independent chains
-      float mq[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-      for (int c = 4; c < kSqdkBN; c += 4) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) mq[u] = fmaxf(mq[u], sv[c + u]);
-      }
-      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      const float m_new = fmaxf(m_run, mx * c2);
-      const bool grow = m_new > m_run + kRescaleLog2;
-      const bool need_o = grow && (m_run != -INFINITY);
-      if (__any_sync(0xFFFFFFFFu, need_o)) {
-        // O holds P_0..P_{j-1} V; PV of block j-1 must have landed first
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_odone, (j - 1) & 1, &abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        const float alpha = need_o ? fast_exp2(m_run - m_new) : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tO + c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tO + c, r);
-        }
-        tmem_wait_st();
-      }
-      if (grow) {
-        l_run *= fast_exp2(m_run - m_new);
-        m_run = m_new;
-      }
-      const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
-      // p = 2^(s*c2 - m): scale with packed FMAs; exp2 on MUFU, and on the FMA
-      // pipe (cubic) for one pair in four of the unmasked blocks, so MUFU is
-      // not the only unit the softmax waits on; row sum with packed adds
-      const uint64_t cc = f2_pack(c2, c2), nm = f2_pack(neg_m, neg_m);
-      uint64_t acc0 = f2_pack(0.0f, 0.0f), acc1 = acc0;
+      // p = 2^(s*c2 - m) with packed FMAs and MUFU exp2, packed to bf16/f16
+      // pairs; the block's row sum is returned
       uint32_t pk[kSqdkBN / 2];
-      if (diag) {
+      auto exponentiate = [&](float m) -> float {
+        const float neg_m = (m == -INFINITY) ? 0.0f : -m;
+        const uint64_t cc = f2_pack(c2, c2), nm = f2_pack(neg_m, neg_m);
+        uint64_t acc0 = f2_pack(0.0f, 0.0f), acc1 = acc0;
 #pragma unroll
         for (int c = 0; c < kSqdkBN; c += 2) {
           float x0, x1;
@@ -335,29 +307,56 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
           else acc0 = f2_add(acc0, f2_pack(p0, p1));
           pk[c >> 1] = pack2<kBF16>(p0, p1);
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kSqdkBN; c += 2) {
-          const uint64_t x = f2_fma(f2_pack(sv[c], sv[c + 1]), cc, nm);
-          float p0, p1;
-          if (((c >> 1) & 3) == 3) {
-            f2_unpack(f2_exp2_poly(x), p0, p1);
-          } else {
-            float x0, x1;
-            f2_unpack(x, x0, x1);
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
-          if ((c >> 1) & 1) acc1 = f2_add(acc1, f2_pack(p0, p1));
-          else acc0 = f2_add(acc0, f2_pack(p0, p1));
-          pk[c >> 1] = pack2<kBF16>(p0, p1);
-        }
-      }
-      {
         float a0, a1, b0, b1;
         f2_unpack(acc0, a0, a1);
         f2_unpack(acc1, b0, b1);
-        l_run += (a0 + a1) + (b0 + b1);
+        return (a0 + a1) + (b0 + b1);
+      };
+      // Optimistic pass: exponentiate against the running maximum without
+      // reducing this block's maximum. Any m works for softmax as long as
+      // nothing overflows; the block's row sum bounds every p of the row, so
+      // a sum below kSqdkSumBound proves the block is representable.
+      bool done = false;
+      if (__all_sync(0xFFFFFFFFu, m_run != -INFINITY)) {
+        const float lb = exponentiate(m_run);
+        if (__all_sync(0xFFFFFFFFu, lb < kSqdkSumBound<kBF16>)) {
+          l_run += lb;
+          done = true;
+        }
+      }
+      if (!done) {
+        // exact pass: this block's row maximum, O rescaled when it grew
+        float mq[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int c = 4; c < kSqdkBN; c += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mq[u] = fmaxf(mq[u], sv[c + u]);
+        }
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        const float m_new = fmaxf(m_run, mx * c2);
+        const bool need_o = j > 0 && (m_run != -INFINITY) && (m_new > m_run);
+        if (__any_sync(0xFFFFFFFFu, need_o)) {
+          // O holds P_0..P_{j-1} V; the PV of block j-1 must have landed first
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_odone, (j - 1) & 1, &abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          const float alpha = need_o ? fast_exp2(m_run - m_new) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tO + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + c, r);
+          }
+          tmem_wait_st();
+        }
+        if (m_new != m_run) {
+          l_run = (m_run == -INFINITY) ? 0.0f : l_run * fast_exp2(m_run - m_new);
+          m_run = m_new;
+        }
+        l_run += exponentiate(m_run);
       }
       tmem_st32(tS + sb * kSqdkBN, pk);
       tmem_wait_st();

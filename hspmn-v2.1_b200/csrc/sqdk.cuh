@@ -219,6 +219,14 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       constexpr uint32_t idesc_s = umma_idesc_f16(kSqdkBM, kSqdkBN, kAB, false, false);
       constexpr uint32_t idesc_o = umma_idesc_f16(kSqdkBM, HD, kAB, false, true);
       const uint32_t tO = tmem + L::kOCol;
+      // shared-memory descriptors built once; a step inside a tile is a
+      // constant added to the 14-bit start-address field (addresses < 256 KB,
+      // so the field never carries)
+      const uint64_t qdesc = sw128_desc(sbase + L::kQOff, 16, 1024);
+      const uint64_t kdesc = sw128_desc(sbase + L::kKOff, 16, 1024);
+      // V block, MN-major: 16 keys = 2 groups of 8 rows (SBO 1024 B), hd in
+      // 64-column chunks L::kKVChunkBytes apart (LBO)
+      const uint64_t vdesc = sw128_desc(sbase + L::kVOff, L::kKVChunkBytes, 1024);
       bool ok = mbar_wait(&bar_q, 0, &abort_flag);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
@@ -226,14 +234,12 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         if (!mbar_wait(&bar_pfull[sb], (jj >> 1) & 1, &abort_flag)) return false;
         if (!mbar_wait(&bar_vfull[s], r & 1, &abort_flag)) return false;
         tc_fence_after();
-        const uint32_t vb = sbase + L::kVOff + s * L::kKVBytes;
+        const uint64_t vd = vdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
+        const uint32_t ta = tmem + sb * kSqdkBN;
+        umma_ts(tO, ta, vd, idesc_o, jj > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < kSqdkBN / 16; ++kk) {
-          // V block, MN-major: 16 keys = 2 groups of 8 rows (SBO 1024 B),
-          // hd in 64-column chunks L::kKVChunkBytes apart (LBO)
-          const uint64_t bdesc = sw128_desc(vb + kk * 16 * 128, L::kKVChunkBytes, 1024);
-          umma_ts(tO, tmem + sb * kSqdkBN + kk * 8, bdesc, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 1; kk < kSqdkBN / 16; ++kk)
+          umma_ts(tO, ta + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_o, 1u);
         umma_commit(&bar_vempty[s]);
         umma_commit(&bar_odone);
         return true;
@@ -242,13 +248,12 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
         if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t kb = sbase + L::kKOff + s * L::kKVBytes;
+        const uint64_t kd = kdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const int c = kk >> 2, w = kk & 3;  // 64-column chunk, 32-byte step inside the swizzle row
-          const uint64_t adesc = sw128_desc(sbase + L::kQOff + c * L::kQChunkBytes + w * 32, 16, 1024);
-          const uint64_t bdesc = sw128_desc(kb + c * L::kKVChunkBytes + w * 32, 16, 1024);
-          umma_ss(tmem + sb * kSqdkBN, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + sb * kSqdkBN, qdesc + static_cast<uint64_t>((c * L::kQChunkBytes + w * 32) >> 4),
+                  kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar_sfull[sb]);
         umma_commit(&bar_kempty[s]);

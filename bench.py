@@ -526,6 +526,8 @@ def run_long(args):
                                    f"kv_heads={args.kv_heads} k={args.sparsity}, zig-zag sequence shards",
                        "seq_len": S, "parallelism": f"sequence-sharded x{world}, all-gather of logits and K/V"},
             "sqdk_ms_per_launch_max_rank": sq_ms, "gpu_launches": launches,
+            "kernels_rank0": {n: {"launches": r["launches"], "ms_per_launch": r["ms"] / max(1, r["launches"])}
+                              for n, r in kres.items()},
             "peak_source": peak_src}), flush=True)
 
 

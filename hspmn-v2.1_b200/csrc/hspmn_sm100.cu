@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -39,6 +40,22 @@ int check_device() {
     __atomic_store_n(&g_arch_ok[dev], state, __ATOMIC_RELEASE);
   }
   return state == 1 ? HSPMN_OK : HSPMN_ERR_DEVICE;
+}
+
+int g_sm_count[kMaxDevices];
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count(int* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HSPMN_ERR_CUDA;
+  int n = __atomic_load_n(&g_sm_count[dev], __ATOMIC_ACQUIRE);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return HSPMN_ERR_CUDA;
+    __atomic_store_n(&g_sm_count[dev], n, __ATOMIC_RELEASE);
+  }
+  *out = n;
+  return HSPMN_OK;
 }
 
 int launch_status() {
@@ -93,10 +110,48 @@ int launch_sqdk(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   auto kern = sqdk_fwd_kernel<HD, kBF16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
     return HSPMN_ERR_CUDA;
-  const int64_t grid = static_cast<int64_t>(prm.T) * prm.B * prm.Hkv;
+  const int64_t tiles = static_cast<int64_t>(prm.T) * prm.B * prm.Hkv;
+  const int64_t grid = tiles * prm.nsplit;
   if (grid > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
   kern<<<static_cast<unsigned>(grid), kSqdkThreads, L::kAlloc, stream>>>(mq, mk, mv, prm);
+  if (prm.nsplit > 1) {
+    if (int rc = launch_status()) return rc;
+    const int64_t warps = tiles * kSqdkBM;
+    sqdk_combine_kernel<HD, kBF16><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(prm);
+  }
   return launch_status();
+}
+
+// Split of each tile's key blocks over several CTAs when a launch has fewer
+// tiles than two per SM: enough CTAs to fill the GPU, at least ~4 blocks of
+// 64 keys per split on average, at most 16 splits.
+struct SqdkPlan {
+  int G, QT, nsplit;
+  int64_t T, tiles, ws_bytes, part_o_bytes;
+};
+
+int sqdk_plan(int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd, SqdkPlan* out) {
+  SqdkPlan pl;
+  pl.G = static_cast<int>(H / Hkv);
+  pl.QT = kSqdkBM / pl.G;
+  pl.T = (K + pl.QT - 1) / pl.QT;
+  pl.tiles = pl.T * B * Hkv;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int64_t target = 2LL * sms;
+  int64_t ns = 1;
+  if (pl.tiles < target) {
+    ns = (target + pl.tiles - 1) / pl.tiles;
+    const int64_t blocks = (S + kSqdkBN - 1) / kSqdkBN;
+    ns = std::min<int64_t>(ns, std::max<int64_t>(1, blocks / 4));
+    ns = std::min<int64_t>(ns, 16);
+  }
+  pl.nsplit = static_cast<int>(ns);
+  const int64_t hdp = hd > 64 ? 128 : 64;
+  pl.part_o_bytes = ns > 1 ? pl.tiles * ns * kSqdkBM * hdp * 4 : 0;
+  pl.ws_bytes = ns > 1 ? pl.part_o_bytes + pl.tiles * ns * kSqdkBM * 2 * 4 : 0;
+  *out = pl;
+  return HSPMN_OK;
 }
 
 template <typename V>
@@ -285,7 +340,7 @@ int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t src_sk, cons
 int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
                    const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
                    const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
-                   int dtype, float sm_scale, void* stream) {
+                   int dtype, float sm_scale, void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !idx || !o || !qs || !ks || !vs || !os) return HSPMN_ERR_INVALID;
   if (B < 0 || K < 0 || S < 1 || H < 1 || Hkv < 1 || !(sm_scale > 0.0f) || !std::isfinite(sm_scale))
     return HSPMN_ERR_INVALID;
@@ -303,9 +358,14 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16)) return HSPMN_ERR_ALIGN;
   if (int rc = check_device()) return rc;
 
-  const int G = static_cast<int>(H / Hkv);
-  const int QT = kSqdkBM / G;
-  const int64_t T = (K + QT - 1) / QT;
+  SqdkPlan pl;
+  if (int rc = sqdk_plan(B, K, S, H, Hkv, hd, &pl)) return rc;
+  if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < static_cast<size_t>(pl.ws_bytes)))
+    return HSPMN_ERR_INVALID;
+  if (pl.ws_bytes > 0 && !aligned(workspace, 16)) return HSPMN_ERR_ALIGN;
+  const int G = pl.G;
+  const int QT = pl.QT;
+  const int64_t T = pl.T;
   const CUtensorMapDataType dt =
       dtype == HSPMN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 
@@ -332,6 +392,9 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   SqdkParams prm;
   prm.idx = idx;
   prm.hd = static_cast<int>(hd);
+  prm.nsplit = pl.nsplit;
+  prm.part_o = pl.ws_bytes > 0 ? static_cast<float*>(workspace) : nullptr;
+  prm.part_ml = pl.ws_bytes > 0 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.part_o_bytes) : nullptr;
   prm.idx_sb = idx_sb;
   prm.idx_sk = idx_sk;
   prm.o = o;
@@ -351,6 +414,13 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   if (hd > 64)
     return dtype == HSPMN_BF16 ? launch_sqdk<128, true>(mq, mk, mv, prm, st) : launch_sqdk<128, false>(mq, mk, mv, prm, st);
   return dtype == HSPMN_BF16 ? launch_sqdk<64, true>(mq, mk, mv, prm, st) : launch_sqdk<64, false>(mq, mk, mv, prm, st);
+}
+
+int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd) {
+  if (B < 1 || K < 1 || S < 1 || H < 1 || Hkv < 1 || H % Hkv != 0 || H / Hkv > kSqdkBM) return 0;
+  SqdkPlan pl;
+  if (sqdk_plan(B, K, S, H, Hkv, hd, &pl) != HSPMN_OK) return -1;
+  return pl.ws_bytes;
 }
 
 int hspmn_device_errors(unsigned* bits, int clear, void* stream) {

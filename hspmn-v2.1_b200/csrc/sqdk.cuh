@@ -70,7 +70,10 @@ struct SqdkLayout {
 
 struct SqdkParams {
   const int64_t* idx;
-  int hd;  // real head_dim (<= the padded tile width HD)
+  int hd;      // real head_dim (<= the padded tile width HD)
+  int nsplit;  // CTAs per tile, each over a contiguous share of the tile's key blocks
+  float* part_o;   // nsplit > 1: [tile*nsplit + split][128][HD] unnormalised fp32 O
+  float* part_ml;  // nsplit > 1: [tile*nsplit + split][128][2] running max (log2 units), row sum
   int64_t idx_sb, idx_sk;
   void* o;
   int64_t o_sb, o_sk, o_sh;  // elements
@@ -99,6 +102,20 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   raise_device_error(HSPMN_DEVERR_TIMEOUT);
 }
 
+// Tile index -> (query tile t, sequence b, kv head g): (sequence, kv-head)
+// pairs in groups of kSqdkPairGroup so the K/V blocks a group streams stay in
+// L2; inside a group the longest query tiles (highest t) come first.
+__device__ __forceinline__ void sqdk_tile_coords(const SqdkParams& p, int tile, int& t, int& b, int& g) {
+  const int BG = p.B * p.Hkv;
+  const int grp = tile / (kSqdkPairGroup * p.T);
+  const int in_grp = tile - grp * kSqdkPairGroup * p.T;
+  const int npairs = min(kSqdkPairGroup, BG - grp * kSqdkPairGroup);
+  t = p.T - 1 - in_grp / npairs;
+  const int bg = grp * kSqdkPairGroup + in_grp % npairs;
+  b = bg / p.Hkv;
+  g = bg % p.Hkv;
+}
+
 template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kSqdkThreads, 2)
     sqdk_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -111,22 +128,16 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   __shared__ __align__(8) uint64_t bar_sfull[2], bar_pfull[2];
   __shared__ __align__(8) uint64_t bar_odone, bar_ofinal, bar_drain;
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int tile_maxpos;
+  __shared__ int warp_maxpos[4];  // largest query position seen by each softmax warp
   __shared__ volatile uint32_t abort_flag;
 
   const uint32_t sbase = (smem_u32(sqdk_smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // tile coordinates: (sequence, kv-head) pairs in groups of kSqdkPairGroup so
-  // the K/V blocks a group streams stay in L2; inside a group the longest
-  // query tiles (highest t) start first
-  const int BG = p.B * p.Hkv;
-  const int grp = static_cast<int>(blockIdx.x) / (kSqdkPairGroup * p.T);
-  const int in_grp = static_cast<int>(blockIdx.x) - grp * kSqdkPairGroup * p.T;
-  const int npairs = min(kSqdkPairGroup, BG - grp * kSqdkPairGroup);
-  const int t = p.T - 1 - in_grp / npairs;
-  const int bg = grp * kSqdkPairGroup + in_grp % npairs;
-  const int b = bg / p.Hkv, g = bg % p.Hkv;
+  const int item = static_cast<int>(blockIdx.x);
+  const int split = item % p.nsplit;
+  int t, b, g;
+  sqdk_tile_coords(p, item / p.nsplit, t, b, g);
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
@@ -143,7 +154,6 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     mbar_init(&bar_odone, 1);
     mbar_init(&bar_ofinal, 1);
     mbar_init(&bar_drain, 1);
-    tile_maxpos = -1;
     abort_flag = 0u;
     fence_mbar_init();
   }
@@ -175,13 +185,19 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       pos = static_cast<int>(ps);
     }
     const int wmax = __reduce_max_sync(0xFFFFFFFFu, pos);
-    if (lane == 0) atomicMax(&tile_maxpos, wmax);
+    if (lane == 0) warp_maxpos[warp & 3] = wmax;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
-  const int nblk = tile_maxpos < 0 ? 0 : tile_maxpos / kSqdkBN + 1;
+  // this CTA's share of the tile's key blocks: [j0, j0 + nblk). Every CTA of
+  // a tile derives the same tile_blocks from the same positions.
+  const int tile_maxpos = max(max(warp_maxpos[0], warp_maxpos[1]), max(warp_maxpos[2], warp_maxpos[3]));
+  const int tile_blocks = tile_maxpos < 0 ? 0 : tile_maxpos / kSqdkBN + 1;
+  const int per_split = (tile_blocks + p.nsplit - 1) / p.nsplit;
+  const int j0 = split * per_split;
+  const int nblk = max(0, min(tile_blocks, j0 + per_split) - j0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -196,13 +212,13 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         mbar_arrive_expect_tx(&bar_kfull[s], L::kKVBytes);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(sbase + L::kKOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmK, &bar_kfull[s], c * 64, g,
-                      j * kSqdkBN, b);
+                      (j0 + j) * kSqdkBN, b);
         ++nk;
         if (r > 0 && !mbar_wait(&bar_vempty[s], (r - 1) & 1, &abort_flag)) break;
         mbar_arrive_expect_tx(&bar_vfull[s], L::kKVBytes);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(sbase + L::kVOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmV, &bar_vfull[s], c * 64, g,
-                      j * kSqdkBN, b);
+                      (j0 + j) * kSqdkBN, b);
         ++nv;
       }
       // every copy this thread issued has landed before the CTA may exit
@@ -289,7 +305,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
           sv[32 + i] = __uint_as_float(r1[i]);
         }
       }
-      const int lim = pos - j * kSqdkBN;  // columns <= lim are visible to this row
+      const int lim = pos - (j0 + j) * kSqdkBN;  // columns <= lim are visible to this row
       // warp-uniform: does any row of this warp need the causal mask here?
       const bool diag = __any_sync(0xFFFFFFFFu, lim < kSqdkBN - 1);
       if (diag) {
@@ -370,37 +386,64 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       if (lane == 0) mbar_arrive(&bar_pfull[sb]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_ofinal, 0, &abort_flag));
+    if (ok && nblk > 0) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_ofinal, 0, &abort_flag));
     using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-    Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
-                static_cast<int64_t>(hh) * p.o_sh;
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l_run;
+    const int r = 32 * (warp & 3) + lane;
+    if (p.nsplit > 1) {
+      // partial result of this share of the key blocks: unnormalised O, the
+      // running maximum it is relative to, and the row sum
+      const int64_t prow = static_cast<int64_t>(item) * kSqdkBM + r;
+      if (ok && nblk > 0) {
+        tc_fence_after();
+        float* dst = p.part_o + prow * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tO + c, r);
-        tmem_wait_ld();
-        if (row_valid) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t rr[32];
+          tmem_ld32(tO + c, rr);
+          tmem_wait_ld();
+          if (row_valid) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            if (c + 8 * v >= p.hd) break;
-            uint4 w;
-            w.x = pack2<kBF16>(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-            w.y = pack2<kBF16>(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-            w.z = pack2<kBF16>(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-            w.w = pack2<kBF16>(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-            dst[v] = w;
+            for (int v = 0; v < 8; ++v)
+              reinterpret_cast<float4*>(dst + c)[v] =
+                  make_float4(__uint_as_float(rr[4 * v]), __uint_as_float(rr[4 * v + 1]),
+                              __uint_as_float(rr[4 * v + 2]), __uint_as_float(rr[4 * v + 3]));
           }
         }
+        if (row_valid) reinterpret_cast<float2*>(p.part_ml)[prow] = make_float2(m_run, l_run);
+      } else if (row_valid) {
+        reinterpret_cast<float2*>(p.part_ml)[prow] = make_float2(-INFINITY, 0.0f);  // nothing in this share
       }
-    } else if (nblk == 0 && row_valid) {
-      // every position in the tile was negative: softmax over nothing
-      const uint32_t nanw = pack2<kBF16>(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000));
-      uint4* dst = reinterpret_cast<uint4*>(orow);
-      for (int v = 0; v < p.hd / 8; ++v) dst[v] = make_uint4(nanw, nanw, nanw, nanw);
+    } else {
+      Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
+                  static_cast<int64_t>(hh) * p.o_sh;
+      if (ok && nblk > 0) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t rr[32];
+          tmem_ld32(tO + c, rr);
+          tmem_wait_ld();
+          if (row_valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              if (c + 8 * v >= p.hd) break;
+              uint4 w;
+              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * inv_l, __uint_as_float(rr[8 * v + 1]) * inv_l);
+              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * inv_l, __uint_as_float(rr[8 * v + 3]) * inv_l);
+              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * inv_l, __uint_as_float(rr[8 * v + 5]) * inv_l);
+              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * inv_l, __uint_as_float(rr[8 * v + 7]) * inv_l);
+              dst[v] = w;
+            }
+          }
+        }
+      } else if (tile_blocks == 0 && row_valid) {
+        // every position in the tile was negative: softmax over nothing
+        const uint32_t nanw = pack2<kBF16>(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000));
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+        for (int v = 0; v < p.hd / 8; ++v) dst[v] = make_uint4(nanw, nanw, nanw, nanw);
+      }
     }
   }
 
@@ -409,6 +452,55 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// Merge of the nsplit partial results of each row (split key ranges):
+//   M = max_s m_s,  w_s = 2^(m_s - M),  o = sum_s w_s O_s / sum_s w_s l_s
+// One warp per (tile, row); lane l owns columns [4l, 4l+4) of each partial.
+template <int HD, bool kBF16>
+__global__ void __launch_bounds__(256) sqdk_combine_kernel(const SqdkParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t ntiles = static_cast<int64_t>(p.T) * p.B * p.Hkv;
+  if (wid >= ntiles * kSqdkBM) return;
+  const int tile = static_cast<int>(wid / kSqdkBM);
+  const int r = static_cast<int>(wid - static_cast<int64_t>(tile) * kSqdkBM);
+  int t, b, g;
+  sqdk_tile_coords(p, tile, t, b, g);
+  const int qloc = r / p.G;
+  const int qi = t * p.QT + qloc;
+  const int hh = g * p.G + (r - qloc * p.G);
+  if (!(qloc < p.QT && qi < p.K)) return;
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
+  float M = -INFINITY;
+  for (int sidx = 0; sidx < p.nsplit; ++sidx)
+    M = fmaxf(M, ml[(static_cast<int64_t>(tile) * p.nsplit + sidx) * kSqdkBM + r].x);
+  float acc[HD / 32];
+#pragma unroll
+  for (int u = 0; u < HD / 32; ++u) acc[u] = 0.0f;
+  float L = 0.0f;
+  for (int sidx = 0; sidx < p.nsplit; ++sidx) {
+    const int64_t prow = (static_cast<int64_t>(tile) * p.nsplit + sidx) * kSqdkBM + r;
+    const float2 v = ml[prow];
+    if (v.x == -INFINITY) continue;  // this share saw no visible key (its O was not written)
+    const float w = fast_exp2(v.x - M);
+    L += w * v.y;
+    const float* po = p.part_o + prow * HD;
+#pragma unroll
+    for (int u = 0; u < HD / 32; ++u) acc[u] += w * po[32 * u + lane];
+  }
+  const float inv_l = 1.0f / L;
+  using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+  Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
+              static_cast<int64_t>(hh) * p.o_sh;
+#pragma unroll
+  for (int u = 0; u < HD / 32; ++u) {
+    const int c = 32 * u + lane;
+    if (c < p.hd) {
+      if constexpr (kBF16) orow[c] = __float2bfloat16_rn(acc[u] * inv_l);
+      else orow[c] = __float2half_rn(acc[u] * inv_l);
+    }
   }
 }
 

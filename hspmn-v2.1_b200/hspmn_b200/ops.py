@@ -365,6 +365,11 @@ def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
         raise TypeError(f"sqdk_fwd: q/k/v dtypes {q.dtype}/{k.dtype}/{v.dtype} unsupported")
     q, k, v = _sqdk_operand(q), _sqdk_operand(k), _sqdk_operand(v)
     o = torch.empty((B, K, H, hd), dtype=q.dtype, device=dev)
+    with _on_device(dev):
+        ws_bytes = int(N.lib().hspmn_sqdk_workspace_size(B, K, S, H, Hkv, hd))
+    if ws_bytes < 0:
+        raise N.HSPMNNativeError("hspmn_sqdk_workspace_size: device query failed")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
     with _on_device(dev), _launch("sqdk_fwd", dev):
         rc = N.lib().hspmn_sqdk_fwd(
             ctypes.c_void_p(q.data_ptr()), N.i64_array(q.stride()),
@@ -372,7 +377,8 @@ def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
             ctypes.c_void_p(v.data_ptr()), N.i64_array(v.stride()),
             ctypes.c_void_p(indices.data_ptr()), indices.stride(0), indices.stride(1),
             ctypes.c_void_p(o.data_ptr()), N.i64_array(o.stride()),
-            B, K, S, H, Hkv, hd, dtype_code(q.dtype), float(sm_scale), _stream(dev))
+            B, K, S, H, Hkv, hd, dtype_code(q.dtype), float(sm_scale),
+            ctypes.c_void_p(ws.data_ptr() if ws is not None else 0), ws_bytes, _stream(dev))
         N.check(rc, "hspmn_sqdk_fwd")
     return o if o.dtype == out_dtype else o.to(out_dtype)
 

@@ -146,6 +146,11 @@ HSPMN_API int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t sr
  * dtype: HSPMN_BF16 or HSPMN_F16 (all of q, k, v, o). hd: a multiple of 8
  * up to 128 (computed on a 64- or 128-wide tile).
  * H % Hkv == 0 and H / Hkv <= 128.
+ * workspace: launches with fewer 128-row tiles than two per SM split each
+ * tile's keys over several CTAs and merge the partial results from a
+ * caller-provided workspace of hspmn_sqdk_workspace_size() bytes (16-byte
+ * aligned; NULL/0 when that size is 0). Launches that overlap on the GPU need
+ * separate workspaces.
  */
 HSPMN_API int hspmn_sqdk_fwd(const void* q, const int64_t* q_strides,
                    const void* k, const int64_t* k_strides,
@@ -153,7 +158,13 @@ HSPMN_API int hspmn_sqdk_fwd(const void* q, const int64_t* q_strides,
                    const int64_t* idx, int64_t idx_sb, int64_t idx_sk,
                    void* o, const int64_t* o_strides,
                    int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
-                   int64_t hd, int dtype, float sm_scale, void* stream);
+                   int64_t hd, int dtype, float sm_scale,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes hspmn_sqdk_fwd needs for this shape on the current device
+ * (0: no split, no workspace; -1: the device could not be queried). */
+HSPMN_API int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H,
+                                            int64_t Hkv, int64_t hd);
 
 /*
  * Read (and optionally clear) the current device's HSPMN_DEVERR_* flag word.

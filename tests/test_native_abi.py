@@ -55,7 +55,7 @@ def test_sqdk_validation_rejects_before_launch():
         a = dict(args, **over)
         return lib.hspmn_sqdk_fwd(a["q"], a["qs"], a["k"], a["ks"], a["v"], a["vs"], a["idx"], a["isb"],
                                   a["isk"], a["o"], a["os_"], a["B"], a["K"], a["S"], a["H"], a["Hkv"],
-                                  a["hd"], a["dt"], ctypes.c_float(a["scale"]), None)
+                                  a["hd"], a["dt"], ctypes.c_float(a["scale"]), None, 0, None)
 
     assert call(q=ctypes.c_void_p(0)) == -1          # null pointer
     assert call(dt=0) == -2                           # float32 not a tensor-core dtype here

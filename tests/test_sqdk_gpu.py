@@ -156,3 +156,17 @@ def test_persistent_many_tiles_per_cta(B, S, H, Hkv, hd, K):
     o, ref = run_case(q, k, v, idx)
     check(o, ref, f"B={B} S={S} H={H} Hkv={Hkv} hd={hd} K={K}")
     assert ops.device_errors() == 0
+
+
+def test_split_workspace_rule_and_parity():
+    """Launches with fewer tiles than two per SM split each tile's keys over
+    several CTAs (partials in a workspace, merged by a second kernel); large
+    launches need no workspace. Both paths match the oracle."""
+    from hspmn_b200 import _native as N
+    lib = N.lib()
+    assert lib.hspmn_sqdk_workspace_size(1, 820, 4096, 16, 4, 128) > 0       # 104 tiles: split
+    assert lib.hspmn_sqdk_workspace_size(64, 820, 4096, 16, 4, 128) == 0     # 6656 tiles: direct
+    for B in (1, 3):
+        q, k, v, idx = make_case(B, 2048, 16, 4, 128, 410, torch.bfloat16, seed=40 + B)
+        o, ref = run_case(q, k, v, idx)
+        check(o, ref, f"B={B}")

@@ -187,6 +187,33 @@ int row_vector_bytes(const void* a, const void* b, int64_t s0, int64_t s1, int64
 }
 
 }  // namespace
+
+// Scratch of hspmn_sqdk_fwd_noalloc: the split-KV partials (unnormalised
+// fp32 O, running max and row sum of each share of a tile's keys) that
+// hspmn_sqdk_fwd keeps in a caller workspace. Part of the module image, so it
+// exists on every device the library's kernels are loaded on; nothing in it
+// needs an initial value, because each call writes every partial it reads.
+static __device__ __align__(256) unsigned char g_sqdk_scratch[HSPMN_SQDK_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_sqdk_scratch_addr[kMaxDevices];
+
+// Device address of g_sqdk_scratch on the current device, looked up on the
+// first call for that device and cached.
+int sqdk_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HSPMN_ERR_CUDA;
+  void* p = __atomic_load_n(&g_sqdk_scratch_addr[dev], __ATOMIC_ACQUIRE);
+  if (!p) {
+    if (cudaGetSymbolAddress(&p, g_sqdk_scratch) != cudaSuccess || !p) return HSPMN_ERR_CUDA;
+    __atomic_store_n(&g_sqdk_scratch_addr[dev], p, __ATOMIC_RELEASE);
+  }
+  *out = p;
+  return HSPMN_OK;
+}
+
+}  // namespace
 }  // namespace hspmn
 
 using namespace hspmn;
@@ -204,6 +231,7 @@ const char* hspmn_strerror(int status) {
     case HSPMN_ERR_UNSUPPORTED: return "head_dim or head grouping not supported";
     case HSPMN_ERR_CUDA: return "CUDA runtime error or launch failure";
     case HSPMN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case HSPMN_ERR_SCRATCH: return "shape needs more split-KV scratch than the no-alloc entry's static buffer holds";
     default: return "unknown status";
   }
 }
@@ -421,6 +449,23 @@ int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H, in
   SqdkPlan pl;
   if (sqdk_plan(B, K, S, H, Hkv, hd, &pl) != HSPMN_OK) return -1;
   return pl.ws_bytes;
+}
+
+int hspmn_sqdk_fwd_noalloc(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                           const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
+                           const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
+                           int dtype, float sm_scale, void* stream) {
+  if (int rc = check_device()) return rc;
+  void* scratch = nullptr;
+  if (int rc = sqdk_scratch(&scratch)) return rc;
+  // hspmn_sqdk_workspace_size gives 0 for shapes hspmn_sqdk_fwd rejects, so
+  // its own validation reports those.
+  const bool shape_ok = B > 0 && K > 0 && S > 0 && hd >= 8 && hd <= 128 && hd % 8 == 0;
+  const int64_t need = shape_ok ? hspmn_sqdk_workspace_size(B, K, S, H, Hkv, hd) : 0;
+  if (need < 0) return HSPMN_ERR_CUDA;
+  if (need > static_cast<int64_t>(HSPMN_SQDK_NOALLOC_SCRATCH_BYTES)) return HSPMN_ERR_SCRATCH;
+  return hspmn_sqdk_fwd(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, B, K, S, H, Hkv, hd, dtype, sm_scale,
+                        need > 0 ? scratch : nullptr, need > 0 ? HSPMN_SQDK_NOALLOC_SCRATCH_BYTES : 0, stream);
 }
 
 int hspmn_device_errors(unsigned* bits, int clear, void* stream) {

@@ -44,7 +44,8 @@ enum hspmn_status {
   HSPMN_ERR_ALIGN = -3,       /* pointer / stride alignment the kernel needs */
   HSPMN_ERR_UNSUPPORTED = -4, /* head_dim or head grouping outside the kernel's range */
   HSPMN_ERR_CUDA = -5,        /* a CUDA runtime call or the launch failed */
-  HSPMN_ERR_DEVICE = -6       /* current device is not an sm_100 part */
+  HSPMN_ERR_DEVICE = -6,      /* current device is not an sm_100 part */
+  HSPMN_ERR_SCRATCH = -7      /* shape needs more scratch than hspmn_sqdk_fwd_noalloc holds */
 };
 
 /* bits of the device-side flag word */
@@ -165,6 +166,46 @@ HSPMN_API int hspmn_sqdk_fwd(const void* q, const int64_t* q_strides,
  * (0: no split, no workspace; -1: the device could not be queried). */
 HSPMN_API int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H,
                                             int64_t Hkv, int64_t hd);
+
+/*
+ * hspmn_sqdk_fwd without a workspace argument; no counterpart in the
+ * reference, which allocates through PyTorch on every call.
+ *
+ * For callers that cannot allocate device memory at the moment they call:
+ * a host without a device allocator of its own behind the C ABI (a plain C,
+ * Go or Java caller that owns only the tensors it passes), or a caller inside
+ * a region where an allocation would synchronise the device or fail. The
+ * split-KV partials go to a static buffer of
+ * HSPMN_SQDK_NOALLOC_SCRATCH_BYTES (32 MiB) that is part of the library's
+ * module on each device; the call itself allocates nothing.
+ *
+ * Arguments, results and error codes are those of hspmn_sqdk_fwd, plus
+ * HSPMN_ERR_SCRATCH, returned without launching anything, for shapes whose
+ * hspmn_sqdk_workspace_size() exceeds HSPMN_SQDK_NOALLOC_SCRATCH_BYTES
+ * (on a 148-SM B200 only launches with hd > 64 and 253 to 295 tiles of 128
+ * rows can be).
+ * Shapes with a workspace size of 0 do not touch the buffer.
+ *
+ * - The first call on each device (with that device current) looks up the
+ *   buffer's device address and caches it; make that first call before any
+ *   stream capture begins. The cached address is not refreshed after a
+ *   cudaDeviceReset.
+ * - Nothing in the buffer has to start at zero: every call writes each
+ *   partial before it reads it.
+ * - There is one buffer per device: calls on the same device whose work can
+ *   overlap on the GPU (different streams without ordering between them, or
+ *   several host threads) race on it and give wrong results. Order them on
+ *   one stream, or use hspmn_sqdk_fwd with separate workspaces.
+ */
+#define HSPMN_SQDK_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+HSPMN_API int hspmn_sqdk_fwd_noalloc(const void* q, const int64_t* q_strides,
+                   const void* k, const int64_t* k_strides,
+                   const void* v, const int64_t* v_strides,
+                   const int64_t* idx, int64_t idx_sb, int64_t idx_sk,
+                   void* o, const int64_t* o_strides,
+                   int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
+                   int64_t hd, int dtype, float sm_scale, void* stream);
 
 /*
  * Read (and optionally clear) the current device's HSPMN_DEVERR_* flag word.

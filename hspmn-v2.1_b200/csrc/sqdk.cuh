@@ -123,10 +123,13 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   using L = SqdkLayout<HD>;
   extern __shared__ uint8_t sqdk_smem_raw[];
   __shared__ __align__(8) uint64_t bar_q;
-  __shared__ __align__(8) uint64_t bar_kfull[kSqdkStages], bar_kempty[kSqdkStages];
+  // K stage j % 2 is free again when Q K^T of block j completes, i.e. when
+  // bar_sfull[j & 1] does: the K ring has no barrier of its own for that
+  static_assert(kSqdkStages == 2, "the K ring reuses the S-buffer barriers");
+  __shared__ __align__(8) uint64_t bar_kfull[kSqdkStages];
   __shared__ __align__(8) uint64_t bar_vfull[kSqdkStages], bar_vempty[kSqdkStages];
   __shared__ __align__(8) uint64_t bar_sfull[2], bar_pfull[2];
-  __shared__ __align__(8) uint64_t bar_odone, bar_ofinal, bar_drain;
+  __shared__ __align__(8) uint64_t bar_ofinal, bar_drain;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int warp_maxpos[4];  // largest query position seen by each softmax warp
   __shared__ volatile uint32_t abort_flag;
@@ -143,7 +146,6 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     mbar_init(&bar_q, 1);
     for (int s = 0; s < kSqdkStages; ++s) {
       mbar_init(&bar_kfull[s], 1);
-      mbar_init(&bar_kempty[s], 1);
       mbar_init(&bar_vfull[s], 1);
       mbar_init(&bar_vempty[s], 1);
     }
@@ -151,7 +153,6 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       mbar_init(&bar_sfull[s], 1);
       mbar_init(&bar_pfull[s], 4);  // one arrival per softmax warp
     }
-    mbar_init(&bar_odone, 1);
     mbar_init(&bar_ofinal, 1);
     mbar_init(&bar_drain, 1);
     abort_flag = 0u;
@@ -205,15 +206,24 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(L::kChunks * p.G * p.QT * 128));
       for (int c = 0; c < L::kChunks; ++c)
         tma_load_4d(sbase + L::kQOff + c * L::kQChunkBytes, &tmQ, &bar_q, c * 64, g * p.G, t * p.QT, b);
+      // K runs one block ahead of V: K_{j+1} is requested (once Q K^T of
+      // block j-1 has freed its stage) before V_j, so a K block never waits
+      // behind a V stage that P V of an older block still holds.
       int nk = 0, nv = 0;
-      for (int j = 0; j < nblk; ++j) {
+      auto load_k = [&](int j) -> bool {
         const int s = j % kSqdkStages, r = j / kSqdkStages;
-        if (r > 0 && !mbar_wait(&bar_kempty[s], (r - 1) & 1, &abort_flag)) break;
+        if (r > 0 && !mbar_wait(&bar_sfull[s], (r - 1) & 1, &abort_flag)) return false;
         mbar_arrive_expect_tx(&bar_kfull[s], L::kKVBytes);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(sbase + L::kKOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmK, &bar_kfull[s], c * 64, g,
                       (j0 + j) * kSqdkBN, b);
         ++nk;
+        return true;
+      };
+      bool live = load_k(0);
+      for (int j = 0; live && j < nblk; ++j) {
+        if (j + 1 < nblk && !load_k(j + 1)) break;
+        const int s = j % kSqdkStages, r = j / kSqdkStages;
         if (r > 0 && !mbar_wait(&bar_vempty[s], (r - 1) & 1, &abort_flag)) break;
         mbar_arrive_expect_tx(&bar_vfull[s], L::kKVBytes);
         for (int c = 0; c < L::kChunks; ++c)
@@ -256,8 +266,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 #pragma unroll
         for (int kk = 1; kk < kSqdkBN / 16; ++kk)
           umma_ts(tO, ta + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_o, 1u);
-        umma_commit(&bar_vempty[s]);
-        umma_commit(&bar_odone);
+        umma_commit(&bar_vempty[s]);  // V stage free, and O holds P_jj V_jj
         return true;
       };
       for (int j = 0; ok && j < nblk; ++j) {
@@ -272,7 +281,6 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
                   kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar_sfull[sb]);
-        umma_commit(&bar_kempty[s]);
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok) ok = issue_pv(nblk - 1);
@@ -358,7 +366,8 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         const bool need_o = j > 0 && (m_run != -INFINITY) && (m_new > m_run);
         if (__any_sync(0xFFFFFFFFu, need_o)) {
           // O holds P_0..P_{j-1} V; the PV of block j-1 must have landed first
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_odone, (j - 1) & 1, &abort_flag));
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_vempty[(j - 1) % kSqdkStages],
+                                                 ((j - 1) / kSqdkStages) & 1, &abort_flag));
           if (!ok) break;
           tc_fence_after();
           const float alpha = need_o ? fast_exp2(m_run - m_new) : 1.0f;

@@ -104,6 +104,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// mbar_wait for two phases at once: both barriers are probed back to back,
+// so the two probe latencies overlap instead of adding up.
+__device__ __forceinline__ bool mbar_wait2(uint64_t* bar1, uint32_t parity1, uint64_t* bar2, uint32_t parity2,
+                                           volatile uint32_t* abort) {
+  bool d1 = mbar_try_wait(bar1, parity1);
+  bool d2 = mbar_try_wait(bar2, parity2);
+  if (d1 && d2) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < kWaitLimitIters; ++it) {
+    if (!d1) d1 = mbar_try_wait(bar1, parity1);
+    if (!d2) d2 = mbar_try_wait(bar2, parity2);
+    if (d1 && d2) return true;
+    if ((it & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  *abort = 1u;
+  raise_device_error(HSPMN_DEVERR_TIMEOUT);
+  return false;
+}
+
 // Named barrier over `nthreads` threads (whole warps) that also ANDs a
 // predicate across them: every participant gets the same result.
 __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {

@@ -255,10 +255,14 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       const uint64_t vdesc = sw128_desc(sbase + L::kVOff, L::kKVChunkBytes, 1024);
       bool ok = mbar_wait(&bar_q, 0, &abort_flag);
       tc_fence_after();
-      auto issue_pv = [&](int jj) -> bool {
+      // P V of block jj; v_landed: V_jj was already waited for
+      auto issue_pv = [&](int jj, bool v_landed) -> bool {
         const int s = jj % kSqdkStages, r = jj / kSqdkStages, sb = jj & 1;
-        if (!mbar_wait(&bar_pfull[sb], (jj >> 1) & 1, &abort_flag)) return false;
-        if (!mbar_wait(&bar_vfull[s], r & 1, &abort_flag)) return false;
+        if (v_landed) {
+          if (!mbar_wait(&bar_pfull[sb], (jj >> 1) & 1, &abort_flag)) return false;
+        } else if (!mbar_wait2(&bar_pfull[sb], (jj >> 1) & 1, &bar_vfull[s], r & 1, &abort_flag)) {
+          return false;
+        }
         tc_fence_after();
         const uint64_t vd = vdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
         const uint32_t ta = tmem + sb * kSqdkBN;
@@ -271,7 +275,15 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       };
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
-        if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) { ok = false; break; }
+        // K_j for this Q K^T and V_{j-1} for the P V after it: requested
+        // together by the producer, so they are waited for together
+        if (j == 0) {
+          if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) { ok = false; break; }
+        } else if (!mbar_wait2(&bar_kfull[s], r & 1, &bar_vfull[(j - 1) % kSqdkStages],
+                               ((j - 1) / kSqdkStages) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint64_t kd = kdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
 #pragma unroll
@@ -281,9 +293,9 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
                   kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar_sfull[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        if (j >= 1 && !issue_pv(j - 1, true)) ok = false;
       }
-      if (ok) ok = issue_pv(nblk - 1);
+      if (ok) ok = issue_pv(nblk - 1, false);
       if (ok) umma_commit(&bar_ofinal);
       umma_commit(&bar_drain);
       mbar_wait_drain(&bar_drain, 0);

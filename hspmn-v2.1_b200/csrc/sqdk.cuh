@@ -273,6 +273,10 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         umma_commit(&bar_vempty[s]);  // V stage free, and O holds P_jj V_jj
         return true;
       };
+      // unrolled by the ring depth: stage, buffer and descriptor offsets
+      // become constants (the issue thread's instruction count per block
+      // bounds the whole pipeline)
+#pragma unroll 2
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
         // K_j for this Q K^T and V_{j-1} for the P V after it: requested

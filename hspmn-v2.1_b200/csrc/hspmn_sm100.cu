@@ -104,8 +104,8 @@ int encode_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const 
 }
 
 template <int HD, bool kBF16>
-int launch_sqdk(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const SqdkParams& prm,
-                cudaStream_t stream) {
+int launch_sqdk(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                const SqdkParams& prm, cudaStream_t stream) {
   using L = SqdkLayout<HD>;
   auto kern = sqdk_fwd_kernel<HD, kBF16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) != cudaSuccess)
@@ -113,7 +113,7 @@ int launch_sqdk(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   const int64_t tiles = static_cast<int64_t>(prm.T) * prm.B * prm.Hkv;
   const int64_t grid = tiles * prm.nsplit;
   if (grid > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
-  kern<<<static_cast<unsigned>(grid), kSqdkThreads, L::kAlloc, stream>>>(mq, mk, mv, prm);
+  kern<<<static_cast<unsigned>(grid), kSqdkThreads, L::kAlloc, stream>>>(mq, mk, mv, mo, prm);
   if (prm.nsplit > 1) {
     if (int rc = launch_status()) return rc;
     const int64_t warps = tiles * kSqdkBM;
@@ -397,7 +397,7 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   const CUtensorMapDataType dt =
       dtype == HSPMN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(H), static_cast<uint64_t>(K),
                               static_cast<uint64_t>(B)};
@@ -405,6 +405,10 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
                              static_cast<uint64_t>(qs[0] * es)};
     const uint32_t box[4] = {64u, static_cast<uint32_t>(G), static_cast<uint32_t>(QT), 1u};
     if (int rc = encode_4d(&mq, q, dt, dims, str, box)) return rc;
+    // the output tile has the query tile's shape; the epilogue stores it with this map
+    const uint64_t ostr[3] = {static_cast<uint64_t>(os[2] * es), static_cast<uint64_t>(os[1] * es),
+                              static_cast<uint64_t>(os[0] * es)};
+    if (int rc = encode_4d(&mo, o, dt, dims, ostr, box)) return rc;
   }
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(Hkv), static_cast<uint64_t>(S),
@@ -440,8 +444,10 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (hd > 64)
-    return dtype == HSPMN_BF16 ? launch_sqdk<128, true>(mq, mk, mv, prm, st) : launch_sqdk<128, false>(mq, mk, mv, prm, st);
-  return dtype == HSPMN_BF16 ? launch_sqdk<64, true>(mq, mk, mv, prm, st) : launch_sqdk<64, false>(mq, mk, mv, prm, st);
+    return dtype == HSPMN_BF16 ? launch_sqdk<128, true>(mq, mk, mv, mo, prm, st)
+                              : launch_sqdk<128, false>(mq, mk, mv, mo, prm, st);
+  return dtype == HSPMN_BF16 ? launch_sqdk<64, true>(mq, mk, mv, mo, prm, st)
+                             : launch_sqdk<64, false>(mq, mk, mv, mo, prm, st);
 }
 
 int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd) {

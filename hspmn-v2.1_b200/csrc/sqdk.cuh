@@ -31,7 +31,8 @@
 // Warp roles (192 threads, two CTAs per SM):
 //   warp 0      TMA producer: Q once, then K_j / V_j through 2-stage rings
 //   warp 1      TMEM allocation + single-thread MMA issue
-//   warps 2..5  softmax, lazy O correction, epilogue (row = TMEM lane)
+//   warps 2..5  softmax, lazy O correction, epilogue (row = TMEM lane): O / l
+//               staged in the freed Q tile, stored by one thread with TMA
 // Every mbarrier wait is bounded (common.cuh); a wait that gives up flags
 // HSPMN_DEVERR_TIMEOUT, tells the other roles to stop, drains what this CTA
 // has in flight and frees its tensor memory before returning.
@@ -51,6 +52,7 @@ constexpr int kSqdkThreads = 192;  // 6 warps
 template <bool kBF16>
 constexpr float kSqdkSumBound = kBF16 ? 1048576.0f : 32768.0f;
 constexpr int kSqdkPairGroup = 8;  // (sequence, kv-head) pairs scheduled together
+constexpr int kSqdkEpilogueBar = 1;  // named barrier of the four softmax warps
 
 template <int HD>
 struct SqdkLayout {
@@ -119,7 +121,8 @@ __device__ __forceinline__ void sqdk_tile_coords(const SqdkParams& p, int tile, 
 template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kSqdkThreads, 2)
     sqdk_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const SqdkParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    const SqdkParams p) {
   using L = SqdkLayout<HD>;
   extern __shared__ uint8_t sqdk_smem_raw[];
   __shared__ __align__(8) uint64_t bar_q;
@@ -162,6 +165,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, L::kTmemCols);
@@ -441,7 +445,11 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     } else {
       Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
                   static_cast<int64_t>(hh) * p.o_sh;
-      if (ok && nblk > 0) {
+      // the four softmax warps agree first (a warp whose wait gave up writes nothing)
+      if (named_bar_and(kSqdkEpilogueBar, 128, ok && nblk > 0)) {
+        // O / l in the Q tile's place (free once the last P V is done), laid out
+        // as the Q load left it: 64-column chunks of 128-byte rows, 16-byte units
+        // XOR-swizzled by row % 8; one thread then stores the tile with TMA
         tc_fence_after();
         const float inv_l = 1.0f / l_run;
 #pragma unroll 1
@@ -449,19 +457,25 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
           uint32_t rr[32];
           tmem_ld32(tO + c, rr);
           tmem_wait_ld();
-          if (row_valid) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          const uint32_t rowb = sbase + L::kQOff + (c >> 6) * L::kQChunkBytes + r * 128;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              if (c + 8 * v >= p.hd) break;
-              uint4 w;
-              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * inv_l, __uint_as_float(rr[8 * v + 1]) * inv_l);
-              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * inv_l, __uint_as_float(rr[8 * v + 3]) * inv_l);
-              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * inv_l, __uint_as_float(rr[8 * v + 5]) * inv_l);
-              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * inv_l, __uint_as_float(rr[8 * v + 7]) * inv_l);
-              dst[v] = w;
-            }
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * inv_l, __uint_as_float(rr[8 * v + 1]) * inv_l);
+            w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * inv_l, __uint_as_float(rr[8 * v + 3]) * inv_l);
+            w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * inv_l, __uint_as_float(rr[8 * v + 5]) * inv_l);
+            w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * inv_l, __uint_as_float(rr[8 * v + 7]) * inv_l);
+            const int unit = ((c & 63) >> 3) + v;  // 16-byte unit in the 128-byte row
+            st_shared_v4(rowb + ((unit ^ (r & 7)) << 4), w);
           }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(kSqdkEpilogueBar, 128);
+        if (warp == 2 && lane == 0) {
+          for (int ch = 0; ch < L::kChunks; ++ch)
+            tma_store_4d(&tmO, sbase + L::kQOff + ch * L::kQChunkBytes, ch * 64, g * p.G, t * p.QT, b);
+          tma_store_commit();
+          tma_store_wait_read();
         }
       } else if (tile_blocks == 0 && row_valid) {
         // every position in the tile was negative: softmax over nothing

@@ -246,19 +246,40 @@ int hspmn_router_topk(const void* logits, int logits_dtype, int64_t logits_rs, c
   if (logits_rs < S || indices_rs < K || (mask && mask_rs < S)) return HSPMN_ERR_INVALID;
   if (B == 0) return HSPMN_OK;
   if (int rc = check_device()) return rc;
-  const int64_t key_bytes = S * (noisy_dtype == HSPMN_F32 ? 4 : 2);
+  // long rows, few of them: one cluster of kRouterClusterCtas CTAs per row
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int nct = (S >= kRouterClusterMinS && B * kRouterClusterCtas <= sms) ? kRouterClusterCtas : 1;
+  const int64_t slice = ((S + nct - 1) / nct + 7) / 8 * 8;
+  const int64_t key_bytes = slice * (noisy_dtype == HSPMN_F32 ? 4 : 2);
+  const bool keys_in_smem = key_bytes <= kRouterSmemKeyBytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (key_bytes <= kRouterSmemKeyBytes) {
-    if (cudaFuncSetAttribute(router_topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kRouterSmemKeyBytes) != cudaSuccess)
-      return HSPMN_ERR_CUDA;
-    router_topk_kernel<true><<<static_cast<unsigned>(B), kRouterThreads, static_cast<size_t>(key_bytes), st>>>(
-        logits, logits_dtype, logits_rs, temp, temp_dtype, noisy_dtype, static_cast<int>(S), static_cast<int>(K),
-        indices, indices_rs, mask, mask_rs);
+  auto kern = keys_in_smem ? router_topk_kernel<true> : router_topk_kernel<false>;
+  const size_t smem = keys_in_smem ? static_cast<size_t>(key_bytes) : 0;
+  if (keys_in_smem &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRouterSmemKeyBytes) != cudaSuccess)
+    return HSPMN_ERR_CUDA;
+  const int Si = static_cast<int>(S), Ki = static_cast<int>(K), slice_i = static_cast<int>(slice);
+  if (nct == 1) {
+    kern<<<static_cast<unsigned>(B), kRouterThreads, smem, st>>>(logits, logits_dtype, logits_rs, temp, temp_dtype,
+                                                                 noisy_dtype, Si, Ki, indices, indices_rs, mask,
+                                                                 mask_rs, slice_i);
   } else {
-    router_topk_kernel<false><<<static_cast<unsigned>(B), kRouterThreads, 0, st>>>(
-        logits, logits_dtype, logits_rs, temp, temp_dtype, noisy_dtype, static_cast<int>(S), static_cast<int>(K),
-        indices, indices_rs, mask, mask_rs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(B * nct));
+    cfg.blockDim = dim3(kRouterThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(nct);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, logits, logits_dtype, logits_rs, temp, temp_dtype, noisy_dtype, Si, Ki,
+                           indices, indices_rs, mask, mask_rs, slice_i) != cudaSuccess)
+      return HSPMN_ERR_CUDA;
   }
   return launch_status();
 }

@@ -1,6 +1,9 @@
 // Router top-K selection (TopKRouter.forward, hspmn_v2_1.py:98,104-105,112-120).
 //
-// One CTA per sequence. Each logit becomes an order-preserving unsigned key
+// One CTA per sequence, or, for a few long sequences, one cluster of
+// kRouterClusterCtas CTAs per sequence, each owning a slice of the row and
+// combining histograms and counts through distributed shared memory.
+// Each logit becomes an order-preserving unsigned key
 // of the rounded `noisy` value (16 bits for bf16/f16, 32 bits for f32); an
 // MSB-first radix select with 256-bin shared-memory histograms finds the K-th
 // largest key T; one pass in position order then keeps every key > T and the
@@ -8,6 +11,8 @@
 // Keys live in shared memory when the row fits, otherwise they are recomputed
 // from the (L2-resident) logits on every pass.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -18,6 +23,10 @@ constexpr int kRouterWarps = kRouterThreads / 32;
 constexpr int kRouterItems = 8;  // consecutive positions per thread per chunk
 constexpr int kRouterChunk = kRouterThreads * kRouterItems;
 constexpr int kRouterSmemKeyBytes = 96 * 1024;
+// rows of at least this many positions, few enough to fill no more than about
+// one wave, are split over a cluster of kRouterClusterCtas CTAs
+constexpr int kRouterClusterMinS = 32768;
+constexpr int kRouterClusterCtas = 8;
 
 __device__ __forceinline__ uint32_t router_key(float logit, float temp, bool divide, int noisy_dtype) {
   const float q = divide ? __fdiv_rn(logit, temp) : logit;
@@ -71,19 +80,33 @@ __device__ __forceinline__ int router_block_scan(int v, int* scratch, int* total
   return excl;
 }
 
+// One row per cluster of `nct` CTAs (an ordinary launch is a cluster of one):
+// CTA `rank` owns positions [rank * slice, (rank + 1) * slice). Every pass
+// combines the CTAs through distributed shared memory between hardware
+// cluster barriers, so nothing waits on a flag and no global scratch is used.
 template <bool kKeysInSmem>
 __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
     const void* __restrict__ logits, int logits_dtype, int64_t logits_rs, const void* __restrict__ temp,
     int temp_dtype, int noisy_dtype, int S, int K, int64_t* __restrict__ indices, int64_t indices_rs,
-    uint8_t* __restrict__ mask, int64_t mask_rs) {
+    uint8_t* __restrict__ mask, int64_t mask_rs, int slice) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) unsigned char router_smem[];
   __shared__ int hist[256];
   __shared__ int scan_scratch[kRouterWarps + 1];
-  __shared__ uint32_t sel_prefix, sel_digit_hi;
+  __shared__ uint32_t sel_digit_hi;
   __shared__ int sel_remaining;
+  __shared__ int slice_gt, slice_eq;  // keys > T and == T in this CTA's slice
 
-  const int b = blockIdx.x;
+  const int nct = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  // a cluster of one (the ordinary launch) needs only block barriers
+  auto sync_all = [&]() {
+    if (nct > 1) cluster.sync(); else __syncthreads();
+  };
+  const int b = static_cast<int>(blockIdx.x) / nct;
   const int tid = threadIdx.x;
+  const int lo = min(S, rank * slice), hi = min(S, lo + slice);
   const bool divide = temp != nullptr;
   const float t = divide ? load_as_float(temp, temp_dtype, 0) : 1.0f;
   const int64_t row = static_cast<int64_t>(b) * logits_rs;
@@ -94,18 +117,18 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
   auto compute_key = [&](int s) -> uint32_t {
     return router_key(load_as_float(logits, logits_dtype, row + s), t, divide, noisy_dtype);
   };
-  auto key_at = [&](int s) -> uint32_t {
+  auto key_at = [&](int s) -> uint32_t {  // s in [lo, hi)
     if constexpr (kKeysInSmem) {
-      return wide ? kcache32[s] : static_cast<uint32_t>(kcache16[s]);
+      return wide ? kcache32[s - lo] : static_cast<uint32_t>(kcache16[s - lo]);
     } else {
       return compute_key(s);
     }
   };
 
   if constexpr (kKeysInSmem) {
-    for (int s = tid; s < S; s += kRouterThreads) {
+    for (int s = lo + tid; s < hi; s += kRouterThreads) {
       const uint32_t k = compute_key(s);
-      if (wide) kcache32[s] = k; else kcache16[s] = static_cast<uint16_t>(k);
+      if (wide) kcache32[s - lo] = k; else kcache16[s - lo] = static_cast<uint16_t>(k);
     }
   }
 
@@ -116,18 +139,33 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
   for (int shift = nbits - 8; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += kRouterThreads) hist[i] = 0;
     __syncthreads();
-    for (int s = tid; s < S; s += kRouterThreads) {
-      const uint32_t k = key_at(s);
-      if ((k & prefix_mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1);
+    // kRouterItems consecutive positions per thread per chunk, all loaded
+    // before any is counted, so each thread keeps several loads in flight
+    for (int c0 = lo; c0 < hi; c0 += kRouterChunk) {
+      const int s0 = c0 + tid * kRouterItems;
+      uint32_t keys[kRouterItems];
+#pragma unroll
+      for (int j = 0; j < kRouterItems; ++j) keys[j] = s0 + j < hi ? key_at(s0 + j) : 0u;
+#pragma unroll
+      for (int j = 0; j < kRouterItems; ++j)
+        if (s0 + j < hi && (keys[j] & prefix_mask) == prefix) atomicAdd(&hist[(keys[j] >> shift) & 0xFFu], 1);
     }
-    __syncthreads();
-    if (tid < 32) {
-      // lane l owns digits [8*(31-l), 8*(31-l)+8): lane 0 the highest ones
+    sync_all();  // every slice histogram is complete
+    if (rank == 0 && tid < 32) {
+      // lane l owns digits [8*(31-l), 8*(31-l)+8): lane 0 the highest ones;
+      // counts summed over the cluster's slices
       const int lane = tid;
       const int base = 8 * (31 - lane);
       int c[8], sum = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { c[j] = hist[base + j]; sum += c[j]; }
+      for (int j = 0; j < 8; ++j) c[j] = 0;
+      for (int r = 0; r < nct; ++r) {
+        const int* h = cluster.map_shared_rank(hist, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[j] += h[base + j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += c[j];
       int incl = sum;  // inclusive scan over lanes = counts of digits >= base
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -149,39 +187,62 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
         }
       }
     }
-    __syncthreads();
-    prefix |= sel_digit_hi << shift;
+    sync_all();  // the selection is published in CTA 0
+    const uint32_t digit = *cluster.map_shared_rank(&sel_digit_hi, 0);
+    remaining = *cluster.map_shared_rank(&sel_remaining, 0);
+    prefix |= digit << shift;
     prefix_mask |= 0xFFu << shift;
-    remaining = sel_remaining;
-    __syncthreads();
+    sync_all();  // everyone has read it before CTA 0 writes the next one
   }
-  (void)sel_prefix;
-  const uint32_t T = prefix;     // K-th largest key
-  const int need_eq = remaining; // how many keys == T are kept (lowest positions first)
+  const uint32_t T = prefix;      // K-th largest key
+  const int need_eq = remaining;  // how many keys == T are kept (lowest positions first)
+
+  // ---- where this slice's output starts ------------------------------------
+  int out_base = 0, eq_base = 0;
+  if (nct > 1) {
+    int n_gt = 0, n_eq = 0;
+    for (int s = lo + tid; s < hi; s += kRouterThreads) {
+      const uint32_t k = key_at(s);
+      n_gt += k > T ? 1 : 0;
+      n_eq += k == T ? 1 : 0;
+    }
+    int tot;
+    router_block_scan(n_gt, scan_scratch, &tot);
+    if (tid == 0) slice_gt = tot;
+    router_block_scan(n_eq, scan_scratch, &tot);
+    if (tid == 0) slice_eq = tot;
+    cluster.sync();
+    for (int r = 0; r < rank; ++r) {  // lower positions live in lower ranks
+      const int g = *cluster.map_shared_rank(&slice_gt, r);
+      const int e = *cluster.map_shared_rank(&slice_eq, r);
+      const int kept = min(e, max(0, need_eq - eq_base));
+      out_base += g + kept;
+      eq_base += e;
+    }
+  }
 
   // ---- compaction in position order --------------------------------------
-  int out_base = 0, eq_base = 0;
   int64_t* out_row = indices + static_cast<int64_t>(b) * indices_rs;
   uint8_t* mask_row = mask ? mask + static_cast<int64_t>(b) * mask_rs : nullptr;
-  for (int c0 = 0; c0 < S; c0 += kRouterChunk) {
+  for (int c0 = lo; c0 < hi; c0 += kRouterChunk) {
     const int s0 = c0 + tid * kRouterItems;
     uint32_t keys[kRouterItems];
-    int n_eq = 0;
+    int n_eq_c = 0;
 #pragma unroll
     for (int j = 0; j < kRouterItems; ++j) {
       const int s = s0 + j;
-      keys[j] = s < S ? key_at(s) : 0u;
-      n_eq += (s < S && keys[j] == T) ? 1 : 0;
+      keys[j] = s < hi ? key_at(s) : 0u;
+      n_eq_c += (s < hi && keys[j] == T) ? 1 : 0;
     }
     int eq_total;
-    const int eq_before = eq_base + router_block_scan(n_eq, scan_scratch, &eq_total);
+    const int eq_before = eq_base + router_block_scan(n_eq_c, scan_scratch, &eq_total);
     bool sel[kRouterItems];
     int n_sel = 0, e = eq_before;
 #pragma unroll
     for (int j = 0; j < kRouterItems; ++j) {
       const int s = s0 + j;
       bool keep = false;
-      if (s < S) {
+      if (s < hi) {
         if (keys[j] > T) keep = true;
         else if (keys[j] == T) { keep = e < need_eq; ++e; }
       }
@@ -193,7 +254,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
 #pragma unroll
     for (int j = 0; j < kRouterItems; ++j) {
       const int s = s0 + j;
-      if (s < S) {
+      if (s < hi) {
         if (sel[j]) out_row[pos++] = s;
         if (mask_row) mask_row[s] = sel[j] ? 1 : 0;
       }
@@ -201,6 +262,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
     out_base += sel_total;
     eq_base += eq_total;
   }
+  if (nct > 1) cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 }  // namespace hspmn

@@ -65,11 +65,35 @@ def test_router_all_equal_selects_first_positions():
 
 
 @pytest.mark.parametrize("S", [65536, 262144])
-def test_router_long_rows_global_key_path(S):
-    """Rows too long for the shared-memory key cache (262144 is the
-    long-context configuration)."""
+def test_router_long_rows_cluster_path(S):
+    """Long rows, few of them: a cluster of CTAs splits each row (262144 is
+    the long-context configuration)."""
     logits = torch.randn(1, S).to(torch.bfloat16)
     run_and_check(logits, 1.0, oracle.router_k(S, 0.2001953125), torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_router_cluster_ties_across_slices(dtype):
+    """Few distinct values, so the K-th largest is tied in every CTA's slice of
+    the row; a row length that leaves the last slice short."""
+    g = torch.Generator().manual_seed(11)
+    logits = (torch.randn(2, 40001, generator=g) * 2).round() / 2
+    for k in (1, 8000, 20001, 40001):
+        run_and_check(logits.to(dtype), None, k, dtype)
+
+
+def test_router_cluster_all_equal():
+    logits = torch.zeros(1, 65536, dtype=torch.bfloat16)
+    idx, _ = run_and_check(logits, 1.0, 13107, torch.bfloat16)
+    assert (idx.cpu()[0] == torch.arange(13107)).all()
+
+
+def test_router_long_rows_global_key_path():
+    """Rows too long for the shared-memory key cache and too many for one
+    cluster each: keys recomputed from the logits on every pass."""
+    g = torch.Generator().manual_seed(5)
+    logits = torch.randn(20, 65536, generator=g)
+    run_and_check(logits, 0.9, 13107, torch.float32)
 
 
 def test_router_strided_logits():

@@ -94,11 +94,24 @@ class ZigZagPlan:
 def _all_gather_rows(local: torch.Tensor, plan: ZigZagPlan, group) -> torch.Tensor:
     """All-gather a [B, 2*chunk, ...] local tensor into the full [B, S, ...]
     sequence in position order (one collective, then one reorder copy)."""
+    return _all_gather_rows_async(local, plan, group)()
+
+
+def _all_gather_rows_async(local: torch.Tensor, plan: ZigZagPlan, group):
+    """Start the all-gather of ``_all_gather_rows``; the returned function
+    makes the current stream wait for it and returns the full tensor. Work
+    queued on the current stream in between overlaps the transfer."""
     W = plan.world
     B = local.shape[0]
+    src = local.contiguous()
     flat = torch.empty((W * B,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(flat, local.contiguous(), group=group)
-    return plan.unshard(list(flat.view((W, B) + tuple(local.shape[1:])).unbind(0)), dim=1)
+    work = dist.all_gather_into_tensor(flat, src, group=group, async_op=True)
+
+    def finish(_src=src) -> torch.Tensor:  # _src: the collective reads it until done
+        work.wait()
+        return plan.unshard(list(flat.view((W, B) + tuple(local.shape[1:])).unbind(0)), dim=1)
+
+    return finish
 
 
 class SequenceShardedBlock:
@@ -184,9 +197,18 @@ class SequenceShardedBlock:
     def _reflexive(self, x_local: torch.Tensor) -> torch.Tensor:
         """ReflexiveStream.forward (hspmn_v2_1.py:141-145) on sharded rows:
         the depthwise conv of each chunk sees its true neighbours."""
-        rf = self.block.reflexive
-        h = rf.norm(x_local)
+        return self._reflexive_end(x_local, *self._reflexive_begin(x_local))
+
+    def _reflexive_begin(self, x_local: torch.Tensor):
+        """Norm and the halo exchange (a collective) of the reflexive stream."""
+        h = self.block.reflexive.norm(x_local)
         before, after = self._halo_rows(h)
+        return h, before, after
+
+    def _reflexive_end(self, x_local: torch.Tensor, h: torch.Tensor, before: torch.Tensor,
+                       after: torch.Tensor) -> torch.Tensor:
+        """Conv over each chunk with its halo rows, SwiGLU MLP, residual."""
+        rf = self.block.reflexive
         c = self.plan.chunk
         outs = []
         for i in range(2):
@@ -208,13 +230,18 @@ class SequenceShardedBlock:
         x_norm = blk.norm(x_local)
         cos, sin = blk.rope(x_local, S)
         pos = self.plan.local_positions(self.rank, device=x_local.device).expand(B, S_local)
-        # K (RoPE at the rows' global positions) and V of the local rows, then
-        # the whole sequence's K/V prefix into local HBM
+        # K (RoPE at the rows' global positions) and V of the local rows
         k_loc = self.ops.rope_gather_rows(blk.k_proj(x_norm).view(B, S_local, Hkv, hd), pos, cos, sin, False)
         v_loc = blk.v_proj(x_norm).view(B, S_local, Hkv, hd)
-        k_full = _all_gather_rows(k_loc.contiguous(), self.plan, self.group)
-        v_full = _all_gather_rows(v_loc.contiguous(), self.plan, self.group)
-        y = self._reflexive(x_local).contiguous()
+        # the reflexive stream's halo exchange goes first: collectives run in
+        # issue order, and it must not queue behind the K/V transfer
+        h, before, after = self._reflexive_begin(x_local)
+        # the whole sequence's K and V into local HBM (each its own contiguous
+        # tensor, which the attention streams fastest), overlapped with the
+        # reflexive MLP and the routed-query work
+        k_finish = _all_gather_rows_async(k_loc, self.plan, self.group)
+        v_finish = _all_gather_rows_async(v_loc, self.plan, self.group)
+        y = self._reflexive_end(x_local, h, before, after).contiguous()
         sel_pos, sel_rows = self._local_selection(ro.indices)
         if sel_pos.shape[1] > 0:
             # the routed queries of this rank: q_proj on those rows only, RoPE at
@@ -223,6 +250,9 @@ class SequenceShardedBlock:
             x_sel = self.ops.gather_rows(x_norm, sel_rows)
             q_sel = blk.q_proj(x_sel).view(B, -1, H, hd)
             q_sel = self.ops.rope_gather_rows(q_sel, sel_pos, cos, sin, False)
+            k_full, v_full = k_finish(), v_finish()
             attn = self.ops.sqdk_fwd(q_sel, k_full, v_full, sel_pos, 1.0 / math.sqrt(hd))
             self.ops.scatter_add_rows_(y, sel_rows, blk.o_proj(attn.reshape(B, -1, D)))
+        else:
+            k_finish(), v_finish()  # every rank takes part in the collectives and waits for them
         return y, ro.aux_loss

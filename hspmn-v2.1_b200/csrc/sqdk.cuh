@@ -53,6 +53,7 @@ template <bool kBF16>
 constexpr float kSqdkSumBound = kBF16 ? 1048576.0f : 32768.0f;
 constexpr int kSqdkPairGroup = 8;  // (sequence, kv-head) pairs scheduled together
 constexpr int kSqdkEpilogueBar = 1;  // named barrier of the four softmax warps
+constexpr int kSqdkLongRange = 32;   // key blocks from which P V goes without its own commit
 
 template <int HD>
 struct SqdkLayout {
@@ -126,9 +127,14 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   using L = SqdkLayout<HD>;
   extern __shared__ uint8_t sqdk_smem_raw[];
   __shared__ __align__(8) uint64_t bar_q;
-  // K stage j % 2 is free again when Q K^T of block j completes, i.e. when
-  // bar_sfull[j & 1] does: the K ring has no barrier of its own for that
-  static_assert(kSqdkStages == 2, "the K ring reuses the S-buffer barriers");
+  // One thread issues every MMA, and they complete in issue order, so
+  // bar_sfull[j & 1] completing (Q K^T of block j done) also means P V of
+  // block j-2 is done: K stage j % 2 (read by that Q K^T) is free again, and
+  // on long key ranges V stage j % 2 (read by that P V) too. There P V needs
+  // no commit of its own except the second-to-last (bar_vempty[0], which no
+  // later Q K^T follows); short ranges, where requesting V after Q K^T rather
+  // than after P V costs more than the commit, keep one per P V.
+  static_assert(kSqdkStages == 2, "the K and V rings reuse the S-buffer barriers");
   __shared__ __align__(8) uint64_t bar_kfull[kSqdkStages];
   __shared__ __align__(8) uint64_t bar_vfull[kSqdkStages], bar_vempty[kSqdkStages];
   __shared__ __align__(8) uint64_t bar_sfull[2], bar_pfull[2];
@@ -203,6 +209,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
   const int per_split = (tile_blocks + p.nsplit - 1) / p.nsplit;
   const int j0 = split * per_split;
   const int nblk = max(0, min(tile_blocks, j0 + per_split) - j0);
+  const bool long_range = nblk >= kSqdkLongRange;  // same for every role of the CTA
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -228,7 +235,10 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       for (int j = 0; live && j < nblk; ++j) {
         if (j + 1 < nblk && !load_k(j + 1)) break;
         const int s = j % kSqdkStages, r = j / kSqdkStages;
-        if (r > 0 && !mbar_wait(&bar_vempty[s], (r - 1) & 1, &abort_flag)) break;
+        // stage s held V_{j-2}: free once its P V is done (or Q K^T of block j, issued after it)
+        if (r > 0 && !(long_range ? mbar_wait(&bar_sfull[s], r & 1, &abort_flag)
+                                  : mbar_wait(&bar_vempty[s], (r - 1) & 1, &abort_flag)))
+          break;
         mbar_arrive_expect_tx(&bar_vfull[s], L::kKVBytes);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(sbase + L::kVOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tmV, &bar_vfull[s], c * 64, g,
@@ -259,14 +269,11 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       const uint64_t vdesc = sw128_desc(sbase + L::kVOff, L::kKVChunkBytes, 1024);
       bool ok = mbar_wait(&bar_q, 0, &abort_flag);
       tc_fence_after();
-      // P V of block jj; v_landed: V_jj was already waited for
-      auto issue_pv = [&](int jj, bool v_landed) -> bool {
+      // P V of block jj once P_jj is written and V_jj has landed (one
+      // overlapped probe of both barriers)
+      auto issue_pv = [&](int jj) -> bool {
         const int s = jj % kSqdkStages, r = jj / kSqdkStages, sb = jj & 1;
-        if (v_landed) {
-          if (!mbar_wait(&bar_pfull[sb], (jj >> 1) & 1, &abort_flag)) return false;
-        } else if (!mbar_wait2(&bar_pfull[sb], (jj >> 1) & 1, &bar_vfull[s], r & 1, &abort_flag)) {
-          return false;
-        }
+        if (!mbar_wait2(&bar_pfull[sb], (jj >> 1) & 1, &bar_vfull[s], r & 1, &abort_flag)) return false;
         tc_fence_after();
         const uint64_t vd = vdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
         const uint32_t ta = tmem + sb * kSqdkBN;
@@ -274,7 +281,8 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 #pragma unroll
         for (int kk = 1; kk < kSqdkBN / 16; ++kk)
           umma_ts(tO, ta + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_o, 1u);
-        umma_commit(&bar_vempty[s]);  // V stage free, and O holds P_jj V_jj
+        if (!long_range) umma_commit(&bar_vempty[s]);
+        else if (jj == nblk - 2) umma_commit(&bar_vempty[0]);  // no Q K^T follows to signal it
         return true;
       };
       // unrolled by the ring depth: stage, buffer and descriptor offsets
@@ -283,12 +291,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 #pragma unroll 2
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
-        // K_j for this Q K^T and V_{j-1} for the P V after it: requested
-        // together by the producer, so they are waited for together
-        if (j == 0) {
-          if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) { ok = false; break; }
-        } else if (!mbar_wait2(&bar_kfull[s], r & 1, &bar_vfull[(j - 1) % kSqdkStages],
-                               ((j - 1) / kSqdkStages) & 1, &abort_flag)) {
+        if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) {
           ok = false;
           break;
         }
@@ -301,9 +304,9 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
                   kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar_sfull[sb]);
-        if (j >= 1 && !issue_pv(j - 1, true)) ok = false;
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
-      if (ok) ok = issue_pv(nblk - 1, false);
+      if (ok) ok = issue_pv(nblk - 1);
       if (ok) umma_commit(&bar_ofinal);
       umma_commit(&bar_drain);
       mbar_wait_drain(&bar_drain, 0);
@@ -385,9 +388,17 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         const float m_new = fmaxf(m_run, mx * c2);
         const bool need_o = j > 0 && (m_run != -INFINITY) && (m_new > m_run);
         if (__any_sync(0xFFFFFFFFu, need_o)) {
-          // O holds P_0..P_{j-1} V; the PV of block j-1 must have landed first
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_vempty[(j - 1) % kSqdkStages],
-                                                 ((j - 1) / kSqdkStages) & 1, &abort_flag));
+          // O holds P_0..P_{j-1} V; the PV of block j-1 must have landed first:
+          // Q K^T of block j+1, issued after it, completes later (and is
+          // the next S this warp waits for anyway)
+          bool landed;
+          if (!long_range)
+            landed = mbar_wait(&bar_vempty[(j - 1) % kSqdkStages], ((j - 1) / kSqdkStages) & 1, &abort_flag);
+          else if (j + 1 < nblk)
+            landed = mbar_wait(&bar_sfull[(j + 1) & 1], ((j + 1) >> 1) & 1, &abort_flag);
+          else
+            landed = mbar_wait(&bar_vempty[0], 0, &abort_flag);
+          ok = __all_sync(0xFFFFFFFFu, landed);
           if (!ok) break;
           tc_fence_after();
           const float alpha = need_o ? fast_exp2(m_run - m_new) : 1.0f;

@@ -5,6 +5,8 @@
 // loads in flight before the stores.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace hspmn {
@@ -143,6 +145,56 @@ __device__ __forceinline__ T rope_elem(T x, T partner, bool low_half, T c, T s) 
   return Elem<T>::r(__fadd_rn(Elem<T>::f(t1), Elem<T>::f(t2)));
 }
 
+// 16-bit element types: the same three roundings with packed 16-bit
+// arithmetic, two elements per instruction. The product of two 16-bit values
+// is exact in fp32, so T(x*c) is the correctly rounded 16-bit product that
+// mul.rn.{bf16,f16}x2 returns; fp32 adds two 16-bit values exactly unless
+// their exponents differ so much that the smaller is far below half a
+// 16-bit ulp, so T(t1 + t2) is the correctly rounded 16-bit sum that
+// add.rn.*x2 returns; and rounding to nearest commutes with negation, so
+// T(-p * s) is the sign-flipped T(p * s). Bit-identical to rope_elem.
+template <bool kBF16>
+__device__ __forceinline__ uint32_t rope_pair16(uint32_t x, uint32_t p, uint32_t c, uint32_t s, uint32_t neg) {
+  uint32_t t1, t2, o;
+  if constexpr (kBF16) {
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t1) : "r"(x), "r"(c));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t2) : "r"(p), "r"(s));
+    t2 ^= neg;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(o) : "r"(t1), "r"(t2));
+  } else {
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(t1) : "r"(x), "r"(c));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(t2) : "r"(p), "r"(s));
+    t2 ^= neg;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(o) : "r"(t1), "r"(t2));
+  }
+  return o;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 rope_vec(uint4 xv, uint4 pv, bool low, uint4 cv, uint4 sv) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value) {
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+    const uint32_t neg = low ? 0x80008000u : 0u;  // rot = -partner in the low half of a head
+    uint4 o;
+    o.x = rope_pair16<kBF16>(xv.x, pv.x, cv.x, sv.x, neg);
+    o.y = rope_pair16<kBF16>(xv.y, pv.y, cv.y, sv.y, neg);
+    o.z = rope_pair16<kBF16>(xv.z, pv.z, cv.z, sv.z, neg);
+    o.w = rope_pair16<kBF16>(xv.w, pv.w, cv.w, sv.w, neg);
+    return o;
+  } else {
+    constexpr int V = 16 / sizeof(T);
+    const T* xa = reinterpret_cast<const T*>(&xv);
+    const T* pa = reinterpret_cast<const T*>(&pv);
+    const T* ca = reinterpret_cast<const T*>(&cv);
+    const T* sa = reinterpret_cast<const T*>(&sv);
+    uint4 ov;
+    T* oa = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int u = 0; u < V; ++u) oa[u] = rope_elem<T>(xa[u], pa[u], low, ca[u], sa[u]);
+    return ov;
+  }
+}
+
 // One warp per selected row; each lane handles groups of 16 bytes (V
 // elements of T) of the output row of H*hd elements. hd is a multiple of
 // 2*V so a group never straddles the two halves of a head.
@@ -178,15 +230,7 @@ __global__ void __launch_bounds__(kRowThreads) rope_gather_rows_kernel(
       const uint4 pv = __ldg(reinterpret_cast<const uint4*>(s + pe));
       const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cr + dd));
       const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sr + dd));
-      const T* xa = reinterpret_cast<const T*>(&xv);
-      const T* pa = reinterpret_cast<const T*>(&pv);
-      const T* ca = reinterpret_cast<const T*>(&cv);
-      const T* sa = reinterpret_cast<const T*>(&sv);
-      uint4 ov;
-      T* oa = reinterpret_cast<T*>(&ov);
-#pragma unroll
-      for (int u = 0; u < V; ++u) oa[u] = rope_elem<T>(xa[u], pa[u], low, ca[u], sa[u]);
-      reinterpret_cast<uint4*>(d)[v] = ov;
+      reinterpret_cast<uint4*>(d)[v] = rope_vec<T>(xv, pv, low, cv, sv);
     }
   }
 }

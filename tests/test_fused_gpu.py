@@ -44,6 +44,27 @@ def test_rope_gather_bit_exact(dtype, H, hd, by_position):
     assert torch.equal(out, ref_t)
 
 
+@pytest.mark.parametrize("dtype,scale", [(torch.bfloat16, 1e-38), (torch.float16, 1e-5), (torch.bfloat16, 3e37),
+                                         (torch.float16, 3e4)])
+def test_rope_gather_subnormal_and_huge(dtype, scale):
+    """Products and sums that land in the type's subnormal range or overflow:
+    the 16-bit paths must round (and saturate) exactly as the reference's ops."""
+    B, S, H, hd, K = 1, 256, 2, 64, 64
+    g = torch.Generator().manual_seed(3)
+    rope = RotaryEmbedding(hd, 512)
+    q = (torch.randn(B, S, H, hd, generator=g) * scale).to(dtype)
+    q[0, :8] = 0.0
+    q[0, 8:16] = -0.0
+    idx = _sorted_idx(B, S, K, g)
+    cos, sin = rope(q, S)
+    out = ops.rope_gather_rows(q.to(DEV), idx.to(DEV), cos.to(DEV), sin.to(DEV), True)
+    qt = q.to(DEV).transpose(1, 2)
+    q_rot, _ = apply_rotary_pos_emb(qt, qt, cos.to(DEV), sin.to(DEV))
+    ref_t = torch.gather(q_rot.transpose(1, 2), 1, idx.to(DEV)[:, :, None, None].expand(-1, -1, H, hd))
+    same = (out.view(torch.int16) == ref_t.view(torch.int16)) | (torch.isnan(out) & torch.isnan(ref_t))
+    assert bool(same.all())
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_scatter_add_rows_bit_exact(dtype):
     B, S, D, K = 3, 500, 256, 100

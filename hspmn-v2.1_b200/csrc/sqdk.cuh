@@ -29,8 +29,12 @@
 // path: block maximum, O and l rescaled, P recomputed.
 //
 // Warp roles (192 threads, two CTAs per SM):
-//   warp 0      TMA producer: Q once, then K_j / V_j through 2-stage rings
-//   warp 1      TMEM allocation + single-thread MMA issue
+//   warp 0      TMA producer: Q once, then K and V through 2-stage rings,
+//               K_{j+1} requested ahead of V_j
+//   warp 1      TMEM allocation + single-thread MMA issue: per block, Q K^T
+//               of block j, one commit, P V of block j-1 (the issuing
+//               thread's steps per block bound the pipeline, so it waits and
+//               commits as little as the ordering allows)
 //   warps 2..5  softmax, lazy O correction, epilogue (row = TMEM lane): O / l
 //               staged in the freed Q tile, stored by one thread with TMA
 // Every mbarrier wait is bounded (common.cuh); a wait that gives up flags

@@ -170,6 +170,17 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     mbar_init(&bar_drain, 1);
     abort_flag = 0u;
     fence_mbar_init();
+    if (p.nsplit == 1) {
+      // an unsplit tile starts at key block 0 whatever its positions: this
+      // thread (the producer) requests Q and K_0 now, so their latency
+      // overlaps the index loads and the barrier below
+      mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(L::kChunks * p.G * p.QT * 128));
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_4d(sbase + L::kQOff + c * L::kQChunkBytes, &tmQ, &bar_q, c * 64, g * p.G, t * p.QT, b);
+      mbar_arrive_expect_tx(&bar_kfull[0], L::kKVBytes);
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_4d(sbase + L::kKOff + c * L::kKVChunkBytes, &tmK, &bar_kfull[0], c * 64, g, 0, b);
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmQ);
@@ -217,14 +228,17 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    const bool early = p.nsplit == 1;  // Q and K_0 already requested in the prologue
     if (lane == 0 && nblk > 0) {
-      mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(L::kChunks * p.G * p.QT * 128));
-      for (int c = 0; c < L::kChunks; ++c)
-        tma_load_4d(sbase + L::kQOff + c * L::kQChunkBytes, &tmQ, &bar_q, c * 64, g * p.G, t * p.QT, b);
+      if (!early) {
+        mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(L::kChunks * p.G * p.QT * 128));
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sbase + L::kQOff + c * L::kQChunkBytes, &tmQ, &bar_q, c * 64, g * p.G, t * p.QT, b);
+      }
       // K runs one block ahead of V: K_{j+1} is requested (once Q K^T of
       // block j-1 has freed its stage) before V_j, so a K block never waits
       // behind a V stage that P V of an older block still holds.
-      int nk = 0, nv = 0;
+      int nk = early ? 1 : 0, nv = 0;
       auto load_k = [&](int j) -> bool {
         const int s = j % kSqdkStages, r = j / kSqdkStages;
         if (r > 0 && !mbar_wait(&bar_sfull[s], (r - 1) & 1, &abort_flag)) return false;
@@ -235,7 +249,7 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         ++nk;
         return true;
       };
-      bool live = load_k(0);
+      bool live = early || load_k(0);
       for (int j = 0; live && j < nblk; ++j) {
         if (j + 1 < nblk && !load_k(j + 1)) break;
         const int s = j % kSqdkStages, r = j / kSqdkStages;
@@ -255,6 +269,10 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         if (nk > s) mbar_wait_drain(&bar_kfull[s], ((nk - 1 - s) / kSqdkStages) & 1);
         if (nv > s) mbar_wait_drain(&bar_vfull[s], ((nv - 1 - s) / kSqdkStages) & 1);
       }
+    } else if (lane == 0 && early) {
+      // a tile without visible keys: drain the prologue's two loads
+      mbar_wait_drain(&bar_q, 0);
+      mbar_wait_drain(&bar_kfull[0], 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue

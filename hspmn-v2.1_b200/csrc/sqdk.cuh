@@ -55,7 +55,7 @@ constexpr int kSqdkThreads = 192;  // 6 warps
 // f16) and O = sum(P V) in fp32 cannot overflow.
 template <bool kBF16>
 constexpr float kSqdkSumBound = kBF16 ? 1048576.0f : 32768.0f;
-constexpr int kSqdkPairGroup = 8;  // (sequence, kv-head) pairs scheduled together
+constexpr int kSqdkPairGroup = 16;  // (sequence, kv-head) pairs scheduled together (16 beat 4, 8 and 32)
 constexpr int kSqdkEpilogueBar = 1;  // named barrier of the four softmax warps
 constexpr int kSqdkLongRange = 32;   // key blocks from which P V goes without its own commit
 

@@ -81,6 +81,46 @@ def test_router_and_rows_validation():
     assert lib.hspmn_scatter_rows(p, 0, 16, p, 9, p, 0, 16, 1, 8, 9, 16, None) == -1
 
 
+def test_rope_and_scatter_add_validation():
+    lib = N.lib()
+    p = ctypes.c_void_p(4096)
+    bf16, bad = 2, 9
+
+    def rope(**o):
+        a = dict(src=p, src_sb=8 * 2 * 128, src_ss=2 * 128, byp=1, idx=p, idx_sb=4, cos=p, sin=p, tab_ss=128,
+                 dst=p, dst_sb=4 * 2 * 128, dst_sk=2 * 128, B=1, S=8, K=4, H=2, hd=128, dt=bf16)
+        a.update(o)
+        return lib.hspmn_rope_gather_rows(a["src"], a["src_sb"], a["src_ss"], a["byp"], a["idx"], a["idx_sb"],
+                                          a["cos"], a["sin"], a["tab_ss"], a["dst"], a["dst_sb"], a["dst_sk"],
+                                          a["B"], a["S"], a["K"], a["H"], a["hd"], a["dt"], None)
+
+    assert rope(src=None) == -1                        # null pointer
+    assert rope(dt=bad) == -2                          # unknown element type
+    assert rope(tab_ss=64) == -1                       # table rows shorter than a head
+    assert rope(idx_sb=-1) == -1
+    assert rope(hd=12, tab_ss=12, src_ss=24, dst_sk=24) == -4  # a 16-byte group would straddle the head halves
+    assert rope(src=ctypes.c_void_p(4098)) == -3       # source not 16-byte aligned
+    assert rope(B=0) == 0 and rope(K=0) == 0           # empty: nothing to do
+
+    def sadd(**o):
+        a = dict(src=p, src_sb=4 * 2048, src_sk=2048, idx=p, idx_sb=4, dst=p, dst_sb=8 * 2048, dst_ss=2048,
+                 B=1, S=8, K=4, row=2048, dt=bf16)
+        a.update(o)
+        return lib.hspmn_scatter_add_rows(a["src"], a["src_sb"], a["src_sk"], a["idx"], a["idx_sb"], a["dst"],
+                                          a["dst_sb"], a["dst_ss"], a["B"], a["S"], a["K"], a["row"], a["dt"], None)
+
+    assert sadd(dst=None) == -1
+    assert sadd(dt=bad) == -2
+    assert sadd(idx_sb=3) == -1                        # index rows shorter than K
+    assert sadd(row=3, src_sk=3, dst_ss=3, src_sb=12, dst_sb=24) == -3  # 6-byte rows
+    assert sadd(B=0) == 0 and sadd(K=0) == 0
+
+    assert lib.hspmn_device_errors(None, 0, None) == -1
+    # workspace size of a shape the attention rejects: 0, no device query
+    assert lib.hspmn_sqdk_workspace_size(1, 8, 64, 4, 3, 128) == 0
+    assert lib.hspmn_strerror(-7).decode().startswith("shape needs more split-KV scratch")
+
+
 def test_ops_reject_cpu_tensors():
     torch = pytest.importorskip("torch")
     from hspmn_b200 import ops

@@ -124,6 +124,24 @@ def test_large_logit_range_rescaling():
     check(o, ref, "rescale")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rescaling_on_long_key_ranges(dtype):
+    """Tiles of 64-128 key blocks (the path where P V needs no commit of its
+    own) with scores that grow along the keys: the running maximum jumps by
+    more than the optimistic bound at many blocks, the last ones included,
+    so O is rescaled mid-tile and at each tile's final block."""
+    B, S, H, Hkv, hd, K = 1, 8192, 4, 4, 128, 512
+    g = torch.Generator().manual_seed(21)
+    q = (torch.randn(B, S, H, hd, generator=g) * 3.0).to(dtype)
+    ramp = torch.linspace(0.1, 8.0 if dtype == torch.bfloat16 else 2.0, S)[None, :, None, None]
+    k = (torch.randn(B, S, Hkv, hd, generator=g) * ramp).to(dtype)
+    v = torch.randn(B, S, Hkv, hd, generator=g).to(dtype)
+    idx = (S // 2 + torch.randperm(S // 2, generator=g)[:K]).sort().values[None]
+    o, ref = run_case(q, k, v, idx)
+    check(o, ref, f"long ranges {dtype}")
+    assert ops.device_errors() == 0
+
+
 def test_cfg5_shape_slice():
     """One sequence of the sparsity-sweep shape (S=32768, H=Hkv=16, hd=128, k=0.05)."""
     S, K = 32768, 1638

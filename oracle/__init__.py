@@ -3,7 +3,7 @@
 TEST INFRASTRUCTURE ONLY. This package restates, in numpy, the reference
 algorithm for router top-K -> gather -> sparse-query dense-key (SQDK) causal
 attention -> scatter, plus the surrounding HSPMNBlock forward. It is the
-checker for the CUDA library: only ``tests/``, ``__graft_entry__.smoke()`` and
+reference the CUDA library is tested against: only ``tests/``, ``__graft_entry__.smoke()`` and
 ``bench.py``'s CPU-baseline / reference arm may import it. The product package
 (``hspmn_b200``) never imports it and has no CPU fallback.
 

@@ -1,6 +1,6 @@
 """The oracle against fixtures produced by the reference itself (CPU only).
 
-These pin the numpy restatement before it is trusted as the checker for the
+These pin the numpy restatement before it is trusted as the oracle for the
 CUDA library: router selections against the reference TopKRouter, SQDK
 against the reference's FlexAttention path (GQA included) and the whole block
 against the reference HSPMNBlock forward.

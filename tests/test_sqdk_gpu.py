@@ -1,6 +1,6 @@
 """SQDK attention kernel vs the fp32 oracle and the reference's Flex goldens.
 
-Tolerance: max |o - o_fp32| <= 2e-2 and
+Tolerance (the path's attention contract): max |o - o_fp32| <= 2e-2 and
 mean |o - o_fp32| <= 2e-3, o computed from bf16/f16 inputs.
 """
 

@@ -382,6 +382,22 @@ def run_block(args):
                    "pipeline": "2-deep: upload of step i+1 and download of step i-1 overlap forward i",
                    "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps}
 
+        # the opt-in fp32 gate kernel next to the module's cuBLAS gate (nn.Linear(dim, 1)),
+        # both over the whole x (larger than L2) of this GPU
+        gate_w, gate_b = model.router.gate.weight, model.router.gate.bias
+        gate_times = {}
+        for name, fn in (("gate_logits", lambda: ops.gate_logits(x, gate_w, gate_b)),
+                         ("cublas_gate", lambda: model.router.gate(x))):
+            for _ in range(3):
+                fn()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record()
+            for _ in range(10):
+                fn()
+            g1.record()
+            torch.cuda.synchronize()
+            gate_times[name] = g0.elapsed_time(g1) / 10
+
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -423,6 +439,13 @@ def run_block(args):
     if "sqdk_fwd" in kernels:
         kernels["sqdk_fwd"]["TFLOP_s"] = achieved
         kernels["sqdk_fwd"]["algorithmic_flops"] = sqdk_flops
+    # gate GEMV: read x and w, write one logit per position (f32 here, bf16 from cuBLAS)
+    gate = {}
+    for name, out_bytes in (("gate_logits", 4), ("cublas_gate", esz)):
+        gb = B * S * D * esz + D * esz + B * S * out_bytes
+        ms = gate_times[name]
+        gate[name] = {"ms_per_launch": ms, "GB_s": gb / (ms / 1e3) / 1e9,
+                      "frac_of_hbm": gb / (ms / 1e3) / 1e9 / float(peaks["hbm_gbs"])}
 
     value = B * S * args.steps * world / (ms_total / 1e3)
     line = {
@@ -436,6 +459,8 @@ def run_block(args):
                      "peak_source": f"{peak_src} bf16 dense, sustained (kernel timed inside a long step)",
                      "flops_per_launch": sqdk_flops, "ms_per_launch": sq_ms, "k_selected": k_sel},
         "kernels": kernels,
+        "router_gate": dict(gate, note="opt-in fp32 gate (router.fp32_gate) vs the default cuBLAS bf16 gate; "
+                                       "outside the timed step"),
         "gpu_launches": launches,
         "clocks": clock_info,
     }

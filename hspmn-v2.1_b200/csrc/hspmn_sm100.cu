@@ -1,6 +1,6 @@
 // C ABI of libhspmn_sm100.so (declared in include/hspmn_sm100.h): argument
 // validation, launch configuration and TMA descriptor encoding for the
-// router, row gather/scatter and SQDK attention kernels. One translation unit
+// router gate and selection, row gather/scatter and SQDK attention kernels. One translation unit
 // so all kernels share the device error word.
 
 #include <cuda.h>
@@ -14,6 +14,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "gate.cuh"
 #include "router.cuh"
 #include "rows.cuh"
 #include "sqdk.cuh"
@@ -228,7 +229,7 @@ const char* hspmn_strerror(int status) {
     case HSPMN_ERR_INVALID: return "invalid argument (null pointer, size or shape)";
     case HSPMN_ERR_DTYPE: return "unsupported element type";
     case HSPMN_ERR_ALIGN: return "pointer or stride alignment not supported";
-    case HSPMN_ERR_UNSUPPORTED: return "head_dim or head grouping not supported";
+    case HSPMN_ERR_UNSUPPORTED: return "head_dim, head grouping or gate row length not supported";
     case HSPMN_ERR_CUDA: return "CUDA runtime error or launch failure";
     case HSPMN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
     case HSPMN_ERR_SCRATCH: return "shape needs more split-KV scratch than the no-alloc entry's static buffer holds";
@@ -281,6 +282,36 @@ int hspmn_router_topk(const void* logits, int logits_dtype, int64_t logits_rs, c
                            indices, indices_rs, mask, mask_rs, slice_i) != cudaSuccess)
       return HSPMN_ERR_CUDA;
   }
+  return launch_status();
+}
+
+int hspmn_gate_logits(const void* x, int x_dtype, int64_t x_sb, int64_t x_ss, const void* weight,
+                      const void* bias, int64_t B, int64_t S, int64_t D, float* logits, int64_t logits_rs,
+                      void* stream) {
+  if (!x || !weight || !logits || B < 0 || S < 1 || D < 1 || x_sb < 0 || x_ss < 0 || logits_rs < S)
+    return HSPMN_ERR_INVALID;
+  if (!valid_dtype(x_dtype)) return HSPMN_ERR_DTYPE;
+  const int64_t es = x_dtype == HSPMN_F32 ? 4 : 2;
+  const int64_t per_vec = 16 / es;
+  if (D % per_vec != 0 || D / per_vec > 0x7FFFFFFF) return HSPMN_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight)) % 16 != 0 ||
+      (x_sb * es) % 16 != 0 || (x_ss * es) % 16 != 0)
+    return HSPMN_ERR_ALIGN;
+  if (B == 0) return HSPMN_OK;
+  if (int rc = check_device()) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  auto kern = x_dtype == HSPMN_F32   ? gate_logits_kernel<float>
+              : x_dtype == HSPMN_F16 ? gate_logits_kernel<__half>
+                                     : gate_logits_kernel<__nv_bfloat16>;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGateThreads, 0) != cudaSuccess || per_sm < 1)
+    return HSPMN_ERR_CUDA;
+  const int64_t need = (B * S + kGateWarps - 1) / kGateWarps;
+  const int64_t grid = std::min<int64_t>(need, static_cast<int64_t>(sms) * per_sm);
+  kern<<<static_cast<unsigned>(grid), kGateThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(x), x_sb * es, x_ss * es, static_cast<const uint4*>(weight), bias, B, S,
+      static_cast<int>(D / per_vec), logits, logits_rs);
   return launch_status();
 }
 

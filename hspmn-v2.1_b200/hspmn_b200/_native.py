@@ -25,6 +25,7 @@ _SIGNATURES = {
     "hspmn_version": (_int, []),
     "hspmn_strerror": (ctypes.c_char_p, [_int]),
     "hspmn_router_topk": (_int, [_vp, _int, _i64, _vp, _int, _int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp]),
+    "hspmn_gate_logits": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "hspmn_gather_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "hspmn_scatter_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "hspmn_sqdk_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp,

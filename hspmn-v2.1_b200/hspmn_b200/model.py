@@ -97,7 +97,13 @@ class TopKRouter(nn.Module):
     the reference; the top-K selection, index sort and mask are one CUDA
     kernel (``ops.router_topk``). Among equal noisy logits the lower position
     is selected first (the reference's ``torch.topk`` leaves that order
-    unspecified)."""
+    unspecified).
+
+    ``fp32_gate`` (off by default): in eval mode the gate GEMV runs as one CUDA
+    kernel (``ops.gate_logits``) that keeps the logits in float32 instead of
+    rounding them to the module dtype; the selection then ranks fp32 values,
+    and ``RouterOutput.logits`` and the auxiliary loss are float32. Training
+    always uses the ``nn.Linear`` gate (its weights need gradients)."""
 
     def __init__(self, dim: int, target_sparsity: float = 0.2, sparsity_coef: float = 0.1,
                  entropy_coef: float = 0.01):
@@ -109,6 +115,7 @@ class TopKRouter(nn.Module):
         self.log_temp = nn.Parameter(torch.zeros(1))
         nn.init.xavier_uniform_(self.gate.weight, gain=0.02)
         nn.init.zeros_(self.gate.bias)
+        self.fp32_gate = False
         self._k_cache_key = None
         self._k_cache_val = 0.0
 
@@ -128,9 +135,16 @@ class TopKRouter(nn.Module):
         dtype (0.2 in bf16 is 0.2001953125: S=4096 selects 820)."""
         return max(1, int(S * self._sparsity_value()))
 
+    def gate_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """``self.gate(x).squeeze(-1)`` (hspmn_v2_1.py:96), or the fp32 gate
+        kernel when ``fp32_gate`` is set and the module is in eval mode."""
+        if self.fp32_gate and not self.training:
+            return ops.gate_logits(x, self.gate.weight, self.gate.bias)
+        return self.gate(x).squeeze(-1)
+
     def forward(self, x: torch.Tensor) -> RouterOutput:
         B, S, _ = x.shape
-        logits = self.gate(x).squeeze(-1)
+        logits = self.gate_logits(x)
         temp = torch.exp(self.log_temp).clamp(0.1, 2.0)
         k = self.num_selected(S)
         if self.training:

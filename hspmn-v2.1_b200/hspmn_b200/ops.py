@@ -188,6 +188,47 @@ def _(logits, temp, k, noisy_dtype):
     return (logits.new_empty((B, k), dtype=torch.int64), logits.new_empty((B, S), dtype=torch.bool))
 
 
+@torch.library.custom_op("hspmn::gate_logits", mutates_args=())
+def gate_logits(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    """TopKRouter's gate (hspmn_v2_1.py:84,96) with float32 logits:
+    ``logits[b,s] = x[b,s,:] . weight + bias`` summed in fp32 in a fixed order
+    and not rounded to x's dtype. ``weight`` is the Linear(dim, 1) weight
+    ([1,D] or [D]), ``bias`` its [1] bias or None; both in x's dtype.
+    Returns float32 [B,S]."""
+    tensors = (x, weight) if bias is None else (x, weight, bias)
+    dev = _require_cuda(*tensors)
+    if x.dim() != 3:
+        raise ValueError(f"gate_logits: x must be [B,S,D], got {tuple(x.shape)}")
+    B, S, D = x.shape
+    if weight.numel() != D:
+        raise ValueError(f"gate_logits: weight has {weight.numel()} elements, expected D={D}")
+    if bias is not None and bias.numel() != 1:
+        raise ValueError("gate_logits: bias must hold one element")
+    if any(t.dtype != x.dtype for t in tensors):
+        raise TypeError("gate_logits: x, weight and bias must share one dtype")
+    es = x.element_size()
+    if x.stride(2) != 1 or (x.stride(0) * es) % 16 or (x.stride(1) * es) % 16 or x.data_ptr() % 16:
+        x = x.contiguous()
+        if x.data_ptr() % 16:
+            x = x.clone()
+    weight = weight.reshape(D)
+    if not weight.is_contiguous() or weight.data_ptr() % 16:
+        weight = weight.clone(memory_format=torch.contiguous_format)
+    logits = torch.empty((B, S), dtype=torch.float32, device=dev)
+    with _on_device(dev), _launch("gate_logits", dev):
+        rc = N.lib().hspmn_gate_logits(
+            ctypes.c_void_p(x.data_ptr()), dtype_code(x.dtype), x.stride(0), x.stride(1),
+            ctypes.c_void_p(weight.data_ptr()), ctypes.c_void_p(bias.data_ptr() if bias is not None else 0),
+            B, S, D, ctypes.c_void_p(logits.data_ptr()), S, _stream(dev))
+        N.check(rc, "hspmn_gate_logits")
+    return logits
+
+
+@gate_logits.register_fake
+def _(x, weight, bias):
+    return x.new_empty(x.shape[:2], dtype=torch.float32)
+
+
 # ---------------------------------------------------------------------------
 # gather / scatter of selected rows
 # ---------------------------------------------------------------------------

@@ -133,7 +133,7 @@ class SequenceShardedBlock:
     # -- router over the gathered logits (hspmn_v2_1.py:95-122, eval) ------
     def _route(self, x_local: torch.Tensor, S: int) -> RouterOutput:
         r = self.block.router
-        logits_local = r.gate(x_local).squeeze(-1)
+        logits_local = r.gate_logits(x_local)
         logits = _all_gather_rows(logits_local, self.plan, self.group)
         temp = torch.exp(r.log_temp).clamp(0.1, 2.0)
         k = r.num_selected(S)

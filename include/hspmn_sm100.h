@@ -2,7 +2,7 @@
  * hspmn_sm100.h - C ABI of libhspmn_sm100.so, the B200 (sm_100a) kernels of
  * the HSPMN v2.1 contextual-stream inference path:
  *
- *   router top-K  ->  gather selected queries  ->  SQDK causal attention
+ *   (fp32 gate ->) router top-K  ->  gather selected queries  ->  SQDK causal attention
  *                 ->  scatter back into the [B,S,D] stream
  *
  * Conventions
@@ -42,7 +42,7 @@ enum hspmn_status {
   HSPMN_ERR_INVALID = -1,     /* null pointer, bad size or shape */
   HSPMN_ERR_DTYPE = -2,       /* element type not supported by this entry point */
   HSPMN_ERR_ALIGN = -3,       /* pointer / stride alignment the kernel needs */
-  HSPMN_ERR_UNSUPPORTED = -4, /* head_dim or head grouping outside the kernel's range */
+  HSPMN_ERR_UNSUPPORTED = -4, /* head_dim, head grouping or gate row length outside the kernel's range */
   HSPMN_ERR_CUDA = -5,        /* a CUDA runtime call or the launch failed */
   HSPMN_ERR_DEVICE = -6,      /* current device is not an sm_100 part */
   HSPMN_ERR_SCRATCH = -7      /* shape needs more scratch than hspmn_sqdk_fwd_noalloc holds */
@@ -76,6 +76,27 @@ HSPMN_API int hspmn_router_topk(const void* logits, int logits_dtype, int64_t lo
                       int64_t B, int64_t S, int64_t K,
                       int64_t* indices, int64_t indices_rs,
                       uint8_t* mask, int64_t mask_rs, void* stream);
+
+/*
+ * Router gate with fp32 logits. Replaces the gate GEMV of TopKRouter.forward,
+ * hspmn_v2_1.py:84,96 (logits = self.gate(x).squeeze(-1)), keeping the sum in
+ * fp32 instead of rounding it to the module dtype:
+ *   logits[b,s] = sum_d x[b,s,d] * weight[d] + bias[0]
+ * Summation order is fixed (per-lane slot accumulators over 16-byte vectors,
+ * a slot tree, a warp xor butterfly, bias last), so each logit depends only
+ * on its row and is reproducible; feed the result to hspmn_router_topk with
+ * logits_dtype HSPMN_F32.
+ * x: [B,S,D] of x_dtype, strides x_sb, x_ss (elements), last dim contiguous.
+ * weight: D contiguous elements of x_dtype; bias: one element of x_dtype or
+ * NULL for 0. logits: float32 [B,S], row stride logits_rs.
+ * Requires D a multiple of 8 (16-bit types) or 4 (f32), x and weight 16-byte
+ * aligned and x_sb, x_ss multiples of 16 bytes (HSPMN_ERR_UNSUPPORTED /
+ * HSPMN_ERR_ALIGN otherwise).
+ */
+HSPMN_API int hspmn_gate_logits(const void* x, int x_dtype, int64_t x_sb, int64_t x_ss,
+                      const void* weight, const void* bias,
+                      int64_t B, int64_t S, int64_t D,
+                      float* logits, int64_t logits_rs, void* stream);
 
 /*
  * Gather of the selected query rows, hspmn_v2_1.py:185-186:

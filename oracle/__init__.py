@@ -21,6 +21,8 @@ from .sqdk_oracle import (  # noqa: F401
     router_k,
     orderable_keys,
     noisy_logits,
+    gate_logits_fp32,
+    gate_error_bound,
     router_topk,
     gather_rows,
     scatter_rows,

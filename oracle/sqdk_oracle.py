@@ -75,6 +75,66 @@ def noisy_logits(logits: np.ndarray, temp: float, dtype: str) -> np.ndarray:
     return round_to(q, dtype)
 
 
+def gate_logits_fp32(x: np.ndarray, w: np.ndarray, bias: float | None, dtype: str) -> np.ndarray:
+    """The router gate ``logits = x . w + b`` (hspmn_v2_1.py:84,96) with float32
+    logits, in the summation order the library defines for it.
+
+    ``x`` [..., D] and ``w`` [D] hold values of ``dtype`` (as float32 arrays);
+    ``bias`` is the bias value or None. Order: the row is cut into vectors of
+    E elements (E = 4 for "f32", 8 for 16-bit types); vector v belongs to
+    lane v % 32, which keeps one float32 accumulator per slot e and adds
+    ``x * w`` to it by a fused multiply-add over its vectors in ascending
+    order; slots are summed as a pairwise tree, the 32 lanes by a xor
+    butterfly (offsets 16, 8, 4, 2, 1), and the bias is added last.
+
+    Each fused multiply-add is formed as a float64 product plus a float64 sum
+    rounded once to float32. For 16-bit inputs that is the exact fma: the
+    product is exact in float32, and the float64 sum is too close to the
+    exact one for the final rounding to differ. For "f32" inputs the float64
+    sum can round before the float32 rounding, so agreement there is to the
+    summation error bound only."""
+    x = np.asarray(x, dtype=F32)
+    w = np.asarray(w, dtype=F32)
+    D = x.shape[-1]
+    E = 4 if dtype == "f32" else 8
+    if D % E:
+        raise ValueError(f"D={D} is not a multiple of {E}")
+    lead = x.shape[:-1]
+    xv = x.reshape(-1, D // E, E).astype(np.float64)
+    wv = w.reshape(D // E, E).astype(np.float64)
+    nvec = D // E
+    R = xv.shape[0]
+    acc = np.zeros((R, 32, E), dtype=F32)
+    for j in range((nvec + 31) // 32):
+        v0, v1 = 32 * j, min(32 * j + 32, nvec)
+        n = v1 - v0
+        prod = xv[:, v0:v1, :] * wv[v0:v1, :]
+        acc[:, :n, :] = (acc[:, :n, :].astype(np.float64) + prod).astype(F32)
+    a = acc
+    if E == 4:
+        t = (a[..., 0] + a[..., 1]) + (a[..., 2] + a[..., 3])
+    else:
+        t = ((a[..., 0] + a[..., 1]) + (a[..., 2] + a[..., 3])) + ((a[..., 4] + a[..., 5]) + (a[..., 6] + a[..., 7]))
+    lanes = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        t = t + t[:, lanes ^ o]
+    out = t[:, 0] + F32(0.0 if bias is None else bias)
+    return out.astype(F32).reshape(lead)
+
+
+def gate_error_bound(x: np.ndarray, w: np.ndarray, bias: float | None) -> np.ndarray:
+    """Upper bound on |fp32 gate logit - exact x . w + b| for any summation
+    order: a sum of D + 1 terms formed by at most D + 1 roundings is off by
+    at most gamma_(D+1) * (sum |x w| + |b|), gamma_n = n u / (1 - n u) with
+    u = 2^-24 (1.01 n u covers it for n u < 0.01), plus 2^-149 per rounding
+    for results in the subnormal range."""
+    x = np.asarray(x, dtype=np.float64)
+    w = np.asarray(w, dtype=np.float64)
+    n = x.shape[-1] + 1
+    mag = np.abs(x) @ np.abs(w) + (0.0 if bias is None else abs(float(bias)))
+    return 1.01 * n * 2.0 ** -24 * mag + n * 2.0 ** -149
+
+
 def orderable_keys(noisy: np.ndarray, dtype: str) -> np.ndarray:
     """Map values to unsigned keys whose integer order is the selection order.
 

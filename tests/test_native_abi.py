@@ -22,7 +22,7 @@ def declared_symbols():
 
 def test_header_declares_entry_points():
     names = declared_symbols()
-    assert {"hspmn_router_topk", "hspmn_gather_rows", "hspmn_scatter_rows", "hspmn_sqdk_fwd"} <= names
+    assert {"hspmn_router_topk", "hspmn_gate_logits", "hspmn_gather_rows", "hspmn_scatter_rows", "hspmn_sqdk_fwd"} <= names
 
 
 def test_library_exports_every_declared_symbol():
@@ -81,6 +81,23 @@ def test_router_and_rows_validation():
     assert lib.hspmn_scatter_rows(p, 0, 16, p, 9, p, 0, 16, 1, 8, 9, 16, None) == -1
 
 
+def test_gate_validation():
+    lib = N.lib()
+    p = ctypes.c_void_p(4096)
+    f32, bf16 = 0, 2
+
+    def gate(x=p, dt=bf16, sb=64 * 256, ss=256, w=p, bias=None, B=1, S=64, D=256, out=p, rs=64):
+        return lib.hspmn_gate_logits(x, dt, sb, ss, w, bias, B, S, D, out, rs, None)
+
+    assert gate(x=None) == -1 and gate(w=None) == -1 and gate(out=None) == -1
+    assert gate(S=0) == -1 and gate(rs=63) == -1 and gate(sb=-1) == -1
+    assert gate(dt=9) == -2
+    assert gate(D=12) == -4 and gate(dt=f32, D=6) == -4      # not whole 16-byte vectors
+    assert gate(x=ctypes.c_void_p(4098)) == -3                # misaligned row base
+    assert gate(ss=260) == -3 and gate(w=ctypes.c_void_p(4104)) == -3
+    assert gate(B=0) == 0                                     # empty: nothing to do
+
+
 def test_rope_and_scatter_add_validation():
     lib = N.lib()
     p = ctypes.c_void_p(4096)
@@ -128,3 +145,5 @@ def test_ops_reject_cpu_tensors():
         ops.router_topk(torch.zeros(1, 8), None, 2, torch.float32)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         ops.gather_rows(torch.zeros(1, 8, 4), torch.zeros(1, 2, dtype=torch.int64))
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ops.gate_logits(torch.zeros(1, 8, 16), torch.zeros(1, 16), None)

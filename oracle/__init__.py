@@ -27,6 +27,7 @@ from .sqdk_oracle import (  # noqa: F401
     gather_rows,
     scatter_rows,
     sqdk_fp32,
+    sqdk_bwd_fp32,
     attention_flops,
     rms_norm,
     rope_tables,

@@ -243,6 +243,51 @@ def sqdk_fp32(q_sel, k, v, idx, sm_scale: float | None = None) -> np.ndarray:
     return out
 
 
+def sqdk_bwd_fp32(q_sel, k, v, idx, d_o, sm_scale: float | None = None):
+    """Gradients of ``sqdk_fp32`` for the output gradient ``d_o`` [B,K,H,hd],
+    in float32: the backward of the reference's training path, whose
+    FlexAttention mask (q_idx >= kv_idx) & mask[b, q_idx] with enable_gqa
+    (hspmn_v2_1.py:200-216) is this attention over the selected rows.
+
+    Per (b, h): P = softmax of the masked scaled scores, O = P V,
+    dP = dO V^T, D = rowsum(dO * O), dS = P (dP - D); dq = scale dS K,
+    dk = scale dS^T Q and dv = P^T dO, dk and dv summed over the query heads
+    that read each key/value head. Returns (dq [B,K,H,hd], dk, dv [B,S,Hkv,hd],
+    lse [B,K,H]), lse the natural-log log-sum-exp of each row's scaled scores."""
+    q_sel = np.asarray(q_sel, dtype=F32)
+    k = np.asarray(k, dtype=F32)
+    v = np.asarray(v, dtype=F32)
+    d_o = np.asarray(d_o, dtype=F32)
+    B, K, H, hd = q_sel.shape
+    S, Hkv = k.shape[1], k.shape[2]
+    G = H // Hkv
+    scale = F32(1.0 / math.sqrt(hd)) if sm_scale is None else F32(sm_scale)
+    dq = np.zeros_like(q_sel)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    lse = np.zeros((B, K, H), dtype=F32)
+    kpos = np.arange(S)
+    for b in range(B):
+        allowed = kpos[None, :] <= idx[b][:, None]
+        for h in range(H):
+            g = h // G
+            s = (q_sel[b, :, h, :] @ k[b, :, g, :].T) * scale
+            s = np.where(allowed, s, -np.inf).astype(F32)
+            m = s.max(axis=1, keepdims=True)
+            p = np.where(allowed, np.exp(s - m), 0.0).astype(F32)
+            l = p.sum(axis=1, keepdims=True)
+            p = p / l
+            lse[b, :, h] = (m + np.log(l))[:, 0]
+            o = p @ v[b, :, g, :]
+            dp = d_o[b, :, h, :] @ v[b, :, g, :].T
+            delta = (d_o[b, :, h, :] * o).sum(axis=1, keepdims=True)
+            ds = p * (dp - delta)
+            dq[b, :, h, :] = scale * (ds @ k[b, :, g, :])
+            dk[b, :, g, :] += scale * (ds.T @ q_sel[b, :, h, :])
+            dv[b, :, g, :] += p.T @ d_o[b, :, h, :]
+    return dq, dk, dv, lse
+
+
 def attention_flops(idx: np.ndarray, H: int, hd: int) -> float:
     """Algorithmic SQDK FLOPs: 2*hd for q.k plus 2*hd for p.v per unmasked
     (query, key) pair, summed over heads: ``4*hd*H*sum(idx+1)``."""

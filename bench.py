@@ -14,7 +14,7 @@ scaling); the timed region is bracketed by barriers and the max over ranks is
 reported.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload block|sqdk-sweep]
+                    [--workload block|sqdk-sweep|sqdk|sqdk-bwd|long]
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy oracle port of HSPMNBlock.forward) on the host cores, one sequence of
@@ -25,6 +25,8 @@ prints one line per k; ``--workload sqdk`` runs the same standalone path at
 ``--batch/--seq-len/--heads/--kv-heads/--sparsity``. ``--workload long`` runs
 one sequence of ``--seq-len`` tokens (262144 for the long-context
 configuration) sequence-sharded over the ranks (strong scaling).
+``--workload sqdk-bwd`` times the SQDK backward (the training path's
+attention gradients) at the block's attention shape.
 """
 
 from __future__ import annotations
@@ -56,7 +58,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "sqdk-sweep", "sqdk", "long"], default="block")
+    ap.add_argument("--workload", choices=["block", "sqdk-sweep", "sqdk", "sqdk-bwd", "long"], default="block")
     ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--dim", type=int, default=2048)
@@ -533,6 +535,66 @@ def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
 
 
 # ---------------------------------------------------------------------------
+# SQDK backward (training path of the contextual stream)
+# ---------------------------------------------------------------------------
+
+
+def run_sqdk_bwd(args):
+    """Backward of the SQDK attention at the block's attention shape
+    (--batch/--seq-len/--heads/--kv-heads/--sparsity, hd = dim / heads): the
+    selected rows of a random sorted selection, the forward with log-sum-exp
+    once, then timed launches of the backward (rowsum(dO*O), the key-block
+    kernel, the dq cast). Algorithmic FLOPs: 10 * hd per (row, visible key)
+    (S^T, dP^T, dV, dK, dQ), i.e. 2.5 x the forward's."""
+    import torch
+
+    from hspmn_b200 import ops
+
+    rank, world, local_rank = dist_env()
+    dev = init_dist(world, local_rank)
+    B, S, H, Hkv = args.batch, args.seq_len, args.heads, args.kv_heads
+    hd = args.dim // H
+    K = max(1, int(S * args.sparsity))
+    peaks, peak_src = load_peaks()
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    q = torch.randn(B, K, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    d_o = torch.randn(B, K, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    idx = torch.sort(torch.rand(B, S, device=dev, generator=g).argsort(dim=1)[:, :K], dim=1)[0]
+    scale = hd ** -0.5
+    with torch.no_grad():
+        o, lse = ops.sqdk_fwd_lse(q, k, v, idx, scale)
+        flops = 10.0 * hd * H * float((idx + 1).sum().item())
+        for _ in range(args.warmup):
+            ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
+        e1.record()
+        torch.cuda.synchronize()
+        assert ops.device_errors(dev) == 0
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+    if rank == 0:
+        tf = flops * world / (ms / 1e3) / 1e12
+        peak = float(peaks["bf16_tflops"])
+        print(json.dumps({
+            "metric": "SQDK backward: attention-gradient TFLOP/s", "value": tf, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic: N(0,1) q/k/v/dO, "
+            "random sorted selection", "config": {"workload": f"SQDK backward B={B} S={S} H={H} Hkv={Hkv} hd={hd} "
+                                                               f"k={args.sparsity} (K={K}) per GPU"},
+            "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / world / peak, "peak_source": f"{peak_src} bf16 dense, burst",
+                         "flops_per_launch": flops}}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # long context: one sequence, sequence-sharded over the ranks
 # ---------------------------------------------------------------------------
 
@@ -616,6 +678,8 @@ def main():
         return run_long(args)
     if args.workload == "sqdk":
         return run_sweep(args, args.batch, args.seq_len, args.heads, args.kv_heads, (args.sparsity,))
+    if args.workload == "sqdk-bwd":
+        return run_sqdk_bwd(args)
     return run_block(args)
 
 

@@ -1,7 +1,8 @@
 // C ABI of libhspmn_sm100.so (declared in include/hspmn_sm100.h): argument
 // validation, launch configuration and TMA descriptor encoding for the
-// router gate and selection, row gather/scatter and SQDK attention kernels. One translation unit
-// so all kernels share the device error word.
+// router gate and selection, row gather/scatter and SQDK attention (forward and
+// backward) kernels. One translation unit so all kernels share the device
+// error word.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -18,6 +19,7 @@
 #include "router.cuh"
 #include "rows.cuh"
 #include "sqdk.cuh"
+#include "sqdk_bwd.cuh"
 
 namespace hspmn {
 namespace {
@@ -417,11 +419,17 @@ int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t src_sk, cons
   return launch_status();
 }
 
-int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
-                   const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
-                   const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
-                   int dtype, float sm_scale, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int sqdk_fwd_impl(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                  const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o, const int64_t* os,
+                  float* lse, int64_t lse_sb, int64_t lse_sk, int64_t B, int64_t K, int64_t S, int64_t H,
+                  int64_t Hkv, int64_t hd, int dtype, float sm_scale, void* workspace, size_t workspace_bytes,
+                  void* stream) {
   if (!q || !k || !v || !idx || !o || !qs || !ks || !vs || !os) return HSPMN_ERR_INVALID;
+  if (lse && (lse_sk < H || lse_sb < 0)) return HSPMN_ERR_INVALID;
   if (B < 0 || K < 0 || S < 1 || H < 1 || Hkv < 1 || !(sm_scale > 0.0f) || !std::isfinite(sm_scale))
     return HSPMN_ERR_INVALID;
   if (dtype != HSPMN_BF16 && dtype != HSPMN_F16) return HSPMN_ERR_DTYPE;
@@ -494,12 +502,193 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
   prm.QT = QT;
   prm.T = static_cast<int>(T);
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  prm.lse = lse;
+  prm.lse_sb = lse_sb;
+  prm.lse_sk = lse_sk;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (hd > 64)
     return dtype == HSPMN_BF16 ? launch_sqdk<128, true>(mq, mk, mv, mo, prm, st)
                               : launch_sqdk<128, false>(mq, mk, mv, mo, prm, st);
   return dtype == HSPMN_BF16 ? launch_sqdk<64, true>(mq, mk, mv, mo, prm, st)
                              : launch_sqdk<64, false>(mq, mk, mv, mo, prm, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                   const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
+                   const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
+                   int dtype, float sm_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  return sqdk_fwd_impl(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, nullptr, 0, 0, B, K, S, H, Hkv, hd, dtype,
+                       sm_scale, workspace, workspace_bytes, stream);
+}
+
+int hspmn_sqdk_fwd_lse(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                       const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
+                       const int64_t* os, float* lse, int64_t lse_sb, int64_t lse_sk, int64_t B, int64_t K,
+                       int64_t S, int64_t H, int64_t Hkv, int64_t hd, int dtype, float sm_scale, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (!lse) return HSPMN_ERR_INVALID;
+  return sqdk_fwd_impl(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, lse, lse_sb, lse_sk, B, K, S, H, Hkv, hd,
+                       dtype, sm_scale, workspace, workspace_bytes, stream);
+}
+
+int64_t hspmn_sqdk_bwd_workspace_size(int64_t B, int64_t K, int64_t H, int64_t hd) {
+  if (B < 1 || K < 1 || H < 1 || hd < 1) return 0;
+  const int64_t delta = (B * K * H * 4 + 255) / 256 * 256;
+  return delta + B * K * H * hd * 4;
+}
+
+int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+                   const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, const void* o,
+                   const int64_t* os, const void* d_o, const int64_t* dos, const float* lse, int64_t lse_sb,
+                   int64_t lse_sk, void* dq, const int64_t* dqs, void* dk, const int64_t* dks, void* dv,
+                   const int64_t* dvs, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
+                   int dtype, float sm_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  // with K == 0 the query-side tensors are empty (their pointers may be null)
+  if (!k || !v || !dk || !dv) return HSPMN_ERR_INVALID;
+  if (!qs || !ks || !vs || !os || !dos || !dqs || !dks || !dvs) return HSPMN_ERR_INVALID;
+  if (B < 0 || K < 0 || S < 1 || H < 1 || Hkv < 1 || !(sm_scale > 0.0f) || !std::isfinite(sm_scale))
+    return HSPMN_ERR_INVALID;
+  if (K > 0 && (!q || !idx || !o || !d_o || !lse || !dq)) return HSPMN_ERR_INVALID;
+  if (dtype != HSPMN_BF16 && dtype != HSPMN_F16) return HSPMN_ERR_DTYPE;
+  if (hd < 8 || hd > kBwdHD || hd % 8 != 0) return HSPMN_ERR_UNSUPPORTED;
+  if (H % Hkv != 0 || H / Hkv > kBwdRows) return HSPMN_ERR_UNSUPPORTED;
+  if (B > 0x7FFFFFFF || K > 0x7FFFFFFF || S > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  if (K > 0 && (lse_sb != K * H || lse_sk != H)) return HSPMN_ERR_INVALID;  // lse dense [B,K,H], like Delta
+  const int64_t es = 2;
+  // key-side tensors always; query-side ones only when there are queries
+  const int64_t* key_s[4] = {ks, vs, dks, dvs};
+  const int64_t* query_s[4] = {qs, os, dos, dqs};
+  for (const int64_t* st : key_s) {
+    if (st[3] != 1) return HSPMN_ERR_ALIGN;
+    for (int i = 0; i < 3; ++i) {
+      if ((st[i] * es) % 16) return HSPMN_ERR_ALIGN;
+      if (st[i] <= 0) return HSPMN_ERR_INVALID;
+    }
+  }
+  if (K > 0) {
+    for (const int64_t* st : query_s) {
+      if (st[3] != 1) return HSPMN_ERR_ALIGN;
+      for (int i = 0; i < 3; ++i)
+        if (st[i] <= 0) return HSPMN_ERR_INVALID;
+    }
+    for (int i = 0; i < 3; ++i)
+      if ((qs[i] * es) % 16 || (dos[i] * es) % 16) return HSPMN_ERR_ALIGN;
+  }
+  // (a null pointer counts as aligned)
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(d_o, 16) || !aligned(dk, 16) ||
+      !aligned(dv, 16))
+    return HSPMN_ERR_ALIGN;
+  if (B == 0) return HSPMN_OK;
+  // K == 0: no query block reaches any key block; the kernel writes zero dK / dV
+  const int64_t need = K > 0 ? hspmn_sqdk_bwd_workspace_size(B, K, H, hd) : 0;
+  if (need > 0 && (!workspace || workspace_bytes < static_cast<size_t>(need))) return HSPMN_ERR_INVALID;
+  if (need > 0 && !aligned(workspace, 16)) return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = static_cast<int>(H / Hkv);
+  const int QTb = kBwdRows / G;
+  float* delta = static_cast<float*>(workspace);
+  float* dq_acc = K > 0 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + (B * K * H * 4 + 255) / 256 * 256)
+                        : nullptr;
+  if (K > 0) {
+    if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(B * K * H * hd * 4), st) != cudaSuccess) return HSPMN_ERR_CUDA;
+    const int64_t rows = B * K * H;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((rows + 7) / 8, static_cast<int64_t>(sms) * 16));
+    if (dtype == HSPMN_BF16)
+      sqdk_bwd_delta_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(o), os[0], os[1], os[2], static_cast<const __nv_bfloat16*>(d_o), dos[0],
+          dos[1], dos[2], delta, static_cast<int>(B), static_cast<int>(K), static_cast<int>(H), static_cast<int>(hd));
+    else
+      sqdk_bwd_delta_kernel<__half><<<grid, 256, 0, st>>>(
+          static_cast<const __half*>(o), os[0], os[1], os[2], static_cast<const __half*>(d_o), dos[0], dos[1], dos[2],
+          delta, static_cast<int>(B), static_cast<int>(K), static_cast<int>(H), static_cast<int>(hd));
+    if (int rc = launch_status()) return rc;
+  }
+  const CUtensorMapDataType dt =
+      dtype == HSPMN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mq, mk, mv, mdo;
+  std::memset(&mq, 0, sizeof(mq));
+  std::memset(&mdo, 0, sizeof(mdo));
+  if (K > 0) {
+    const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(H), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(B)};
+    const uint32_t box[4] = {64u, static_cast<uint32_t>(G), static_cast<uint32_t>(QTb), 1u};
+    const uint64_t sq[3] = {static_cast<uint64_t>(qs[2] * es), static_cast<uint64_t>(qs[1] * es),
+                            static_cast<uint64_t>(qs[0] * es)};
+    const uint64_t sd[3] = {static_cast<uint64_t>(dos[2] * es), static_cast<uint64_t>(dos[1] * es),
+                            static_cast<uint64_t>(dos[0] * es)};
+    if (int rc = encode_4d(&mq, q, dt, dims, sq, box)) return rc;
+    if (int rc = encode_4d(&mdo, d_o, dt, dims, sd, box)) return rc;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(Hkv), static_cast<uint64_t>(S),
+                              static_cast<uint64_t>(B)};
+    const uint32_t box[4] = {64u, 1u, static_cast<uint32_t>(kBwdKeys), 1u};
+    const uint64_t sk[3] = {static_cast<uint64_t>(ks[2] * es), static_cast<uint64_t>(ks[1] * es),
+                            static_cast<uint64_t>(ks[0] * es)};
+    const uint64_t sv[3] = {static_cast<uint64_t>(vs[2] * es), static_cast<uint64_t>(vs[1] * es),
+                            static_cast<uint64_t>(vs[0] * es)};
+    if (int rc = encode_4d(&mk, k, dt, dims, sk, box)) return rc;
+    if (int rc = encode_4d(&mv, v, dt, dims, sv, box)) return rc;
+  }
+  SqdkBwdParams prm;
+  prm.idx = idx;
+  prm.idx_sb = idx_sb;
+  prm.idx_sk = idx_sk;
+  prm.lse = lse;
+  prm.delta = delta;
+  prm.row_sb = K * H;
+  prm.row_sk = H;
+  prm.dq = dq_acc;
+  prm.dq_sb = K * H * hd;
+  prm.dq_sk = H * hd;
+  prm.dq_sh = hd;
+  prm.dk = dk;
+  prm.dv = dv;
+  prm.dk_sb = dks[0];
+  prm.dk_ss = dks[1];
+  prm.dk_sh = dks[2];
+  prm.dv_sb = dvs[0];
+  prm.dv_ss = dvs[1];
+  prm.dv_sh = dvs[2];
+  prm.B = static_cast<int>(B);
+  prm.K = static_cast<int>(K);
+  prm.S = static_cast<int>(S);
+  prm.H = static_cast<int>(H);
+  prm.Hkv = static_cast<int>(Hkv);
+  prm.G = G;
+  prm.QTb = QTb;
+  prm.hd = static_cast<int>(hd);
+  prm.nkb = static_cast<int>((S + kBwdKeys - 1) / kBwdKeys);
+  prm.scale = sm_scale;
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  const int64_t grid = static_cast<int64_t>(prm.nkb) * B * Hkv;
+  if (grid > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  auto kern = dtype == HSPMN_BF16 ? sqdk_bwd_kernel<true> : sqdk_bwd_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SqdkBwdLayout::kAlloc) != cudaSuccess)
+    return HSPMN_ERR_CUDA;
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, SqdkBwdLayout::kAlloc, st>>>(mq, mk, mv, mdo, prm);
+  if (int rc = launch_status()) return rc;
+  if (K > 0) {
+    const int64_t n = B * K * H * hd;
+    const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sms) * 32));
+    if (dtype == HSPMN_BF16)
+      sqdk_bwd_dq_cast_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>(dq_acc, static_cast<__nv_bfloat16*>(dq), dqs[0],
+                                                                  dqs[1], dqs[2], static_cast<int>(B),
+                                                                  static_cast<int>(K), static_cast<int>(H),
+                                                                  static_cast<int>(hd));
+    else
+      sqdk_bwd_dq_cast_kernel<__half><<<g2, 256, 0, st>>>(dq_acc, static_cast<__half*>(dq), dqs[0], dqs[1], dqs[2],
+                                                           static_cast<int>(B), static_cast<int>(K),
+                                                           static_cast<int>(H), static_cast<int>(hd));
+  }
+  return launch_status();
 }
 
 int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd) {

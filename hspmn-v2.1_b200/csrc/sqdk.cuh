@@ -86,7 +86,11 @@ struct SqdkParams {
   int64_t o_sb, o_sk, o_sh;  // elements
   int B, K, S, H, Hkv, G, QT, T;
   float scale_log2;
+  float* lse;  // optional [B,K,H] (strides lse_sb, lse_sk, 1): natural-log log-sum-exp of each row's scores
+  int64_t lse_sb, lse_sk;
 };
+
+constexpr float kLn2 = 0.69314718055994531f;
 
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -485,6 +489,9 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
         // XOR-swizzled by row % 8; one thread then stores the tile with TMA
         tc_fence_after();
         const float inv_l = 1.0f / l_run;
+        if (p.lse && row_valid)
+          p.lse[static_cast<int64_t>(b) * p.lse_sb + static_cast<int64_t>(qi) * p.lse_sk + hh] =
+              (m_run + log2f(l_run)) * kLn2;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           uint32_t rr[32];
@@ -563,6 +570,8 @@ __global__ void __launch_bounds__(256) sqdk_combine_kernel(const SqdkParams p) {
     for (int u = 0; u < HD / 32; ++u) acc[u] += w * po[32 * u + lane];
   }
   const float inv_l = 1.0f / L;
+  if (p.lse && lane == 0)
+    p.lse[static_cast<int64_t>(b) * p.lse_sb + static_cast<int64_t>(qi) * p.lse_sk + hh] = (M + log2f(L)) * kLn2;
   using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   Elt* orow = static_cast<Elt*>(p.o) + static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qi) * p.o_sk +
               static_cast<int64_t>(hh) * p.o_sh;

@@ -1,0 +1,489 @@
+// Backward of the sparse-query dense-key causal attention on tcgen05 / TMEM /
+// TMA (sm_100a): gradients of sqdk_fwd_kernel's output with respect to the
+// selected queries, the keys and the values. The reference trains this path
+// through FlexAttention's backward (hspmn_v2_1.py:200-216, mask
+// (q_idx >= kv_idx) & mask[b, q_idx], GQA as enable_gqa).
+//
+// Work unit: one sequence b, one K/V head g and a block of 128 keys
+// [n0, n0 + 128). The CTA walks the query blocks that can see these keys:
+// 64 rows (query, head) r = q * G + h of head group g (the order a TMA box
+// over [B,K,H,hd] lands in shared memory), for the queries whose positions
+// reach n0 (indices are sorted: a suffix of the query list). Per block j:
+//   S^T  = K Q^T       tcgen05.mma SS, M=128 keys, N=64 rows, K=hd
+//   dP^T = V dO^T      tcgen05.mma SS, same shape
+//   P^T  = 2^(S^T c - lse2),  dS^T = scale P^T (dP^T - Delta)
+//                      one thread per key (TMEM lane); P^T and dS^T go back to
+//                      TMEM as 16-bit operands, dS^T also to shared memory
+//   dV  += P^T dO      tcgen05.mma TS (A = P^T in TMEM, B = dO MN-major)
+//   dK  += dS^T Q      tcgen05.mma TS (A = dS^T in TMEM, B = Q MN-major)
+//   dQ^T = K^T dS      tcgen05.mma SS (A = K MN-major, B = dS MN-major), into
+//                      the columns dP^T used; added into an fp32 dQ in global
+//                      memory (other key blocks add to the same rows)
+// dK and dV accumulate in TMEM over all query blocks and are stored once.
+//
+// TMEM (512 columns, one CTA per SM): two sets of [S^T | dP^T] (64 + 64
+// columns; block j uses set j % 2, so the next block's S^T and dP^T overlap
+// this block's softmax), dV (128), dK (128).
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer: K and V once, Q_j and dO_j through a 2-stage
+//               ring; writes each block's per-row data (position, lse, Delta)
+//   warp 1      TMEM allocation + single-thread MMA issue
+//   warps 2..5  P^T / dS^T (thread = key), then the dK / dV epilogue
+//   warps 6..9  dQ: TMEM -> registers -> fp32 reductions (thread = column d)
+// Every mbarrier wait is bounded; a wait that gives up flags
+// HSPMN_DEVERR_TIMEOUT, the other roles stop, and the CTA drains its copies
+// and MMAs and frees its tensor memory before returning. TMEM loads and
+// stores are warp-collective: every lane of a warp issues them, and only the
+// global stores that follow depend on the lane.
+#pragma once
+
+#include "common.cuh"
+#include "sqdk.cuh"
+
+namespace hspmn {
+
+constexpr int kBwdKeys = 128;   // keys per CTA (M of the key-major products)
+constexpr int kBwdRows = 64;    // rows (query, head) per query block
+constexpr int kBwdThreads = 320;
+constexpr int kBwdHD = 128;     // head_dim tile (hd <= 128; columns past hd are zero)
+
+struct SqdkBwdLayout {
+  static constexpr int kChunks = kBwdHD / 64;
+  static constexpr int kKVChunkBytes = kBwdKeys * 128;   // 16 KB: 128 rows x 128 B
+  static constexpr int kKVBytes = kChunks * kKVChunkBytes;
+  static constexpr int kRowChunkBytes = kBwdRows * 128;  // 8 KB
+  static constexpr int kRowBytes = kChunks * kRowChunkBytes;
+  static constexpr int kDSBytes = kBwdKeys * 128;        // 128 keys x 64 rows x 2 B
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kKVBytes;
+  static constexpr int kQOff = kVOff + kKVBytes;
+  static constexpr int kDOOff = kQOff + 2 * kRowBytes;
+  static constexpr int kDSOff = kDOOff + 2 * kRowBytes;
+  static constexpr int kBytes = kDSOff + 2 * kDSBytes;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kSetCols = 128;  // S^T at +0, dP^T / dQ^T at +64
+  static constexpr int kDVCol = 256;
+  static constexpr int kDKCol = 384;
+};
+
+struct SqdkBwdParams {
+  const int64_t* idx;
+  int64_t idx_sb, idx_sk;
+  const float* lse;    // [B,K,H] natural-log log-sum-exp from the forward
+  const float* delta;  // [B,K,H] rowsum(dO * O)
+  int64_t row_sb, row_sk;  // strides of lse / delta (elements; head stride 1)
+  float* dq;           // fp32 [B,K,H,hd] accumulator (zeroed by the host)
+  int64_t dq_sb, dq_sk, dq_sh;
+  void* dk;
+  void* dv;
+  int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
+  int B, K, S, H, Hkv, G, QTb, hd, nkb;
+  float scale, scale_log2;
+};
+
+// Block index -> (key block kb, sequence b, kv head g); low key blocks (the
+// ones most queries see) first.
+__device__ __forceinline__ void sqdk_bwd_coords(const SqdkBwdParams& p, int item, int& kb, int& b, int& g) {
+  const int BG = p.B * p.Hkv;
+  kb = item / BG;
+  const int bg = item - kb * BG;
+  b = bg / p.Hkv;
+  g = bg - b * p.Hkv;
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    sqdk_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const SqdkBwdParams p) {
+  using L = SqdkBwdLayout;
+  extern __shared__ uint8_t sqdk_bwd_smem_raw[];
+  __shared__ __align__(8) uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_pfull[2];
+  __shared__ __align__(8) uint64_t bar_dqfull[2], bar_setfree[2], bar_final, bar_drain;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int first_block_sh, nblk_sh;
+  __shared__ int info_pos[2][kBwdRows];
+  __shared__ float info_lse2[2][kBwdRows], info_delta[2][kBwdRows];
+  __shared__ int row_q[kBwdRows], row_off[kBwdRows];  // per row: query offset in the block (-1: none), dq offset
+  __shared__ volatile uint32_t abort_flag;
+
+  const uint32_t sbase = (smem_u32(sqdk_bwd_smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int kb, b, g;
+  sqdk_bwd_coords(p, static_cast<int>(blockIdx.x), kb, b, g);
+  const int n0 = kb * kBwdKeys;
+  const int nqb = (p.K + p.QTb - 1) / p.QTb;  // query blocks of the whole sequence
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_kv, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_qfull[s], 1);
+      mbar_init(&bar_qempty[s], 1);
+      mbar_init(&bar_sfull[s], 1);
+      mbar_init(&bar_pfull[s], 4);
+      mbar_init(&bar_dqfull[s], 1);
+      mbar_init(&bar_setfree[s], 4);
+    }
+    mbar_init(&bar_final, 1);
+    mbar_init(&bar_drain, 1);
+    abort_flag = 0u;
+    fence_mbar_init();
+    // first query whose position reaches n0 (positions ascend along the row)
+    const int64_t* ib = p.idx + static_cast<int64_t>(b) * p.idx_sb;
+    int lo = 0, hi = p.K;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(ib + static_cast<int64_t>(mid) * p.idx_sk) < n0) lo = mid + 1;
+      else hi = mid;
+    }
+    first_block_sh = lo / p.QTb;
+    nblk_sh = lo < p.K ? nqb - lo / p.QTb : 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, L::kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x < kBwdRows) {
+    const int c = threadIdx.x, qloc = c / p.G;
+    row_q[c] = qloc < p.QTb ? qloc : -1;
+    row_off[c] = static_cast<int>(qloc * p.dq_sk + (g * p.G + c - qloc * p.G) * p.dq_sh);
+  }
+  // rows of the query tiles past G * QTb are never written by TMA: zero them
+  // once, so the row sums of dV / dK see exact zeros there
+  {
+    const int used = p.G * p.QTb;
+    if (used < kBwdRows) {
+      for (int i = threadIdx.x; i < 2 * 2 * L::kChunks * (kBwdRows - used) * 8; i += kBwdThreads) {
+        const int unit = i & 7;
+        int rest = i >> 3;
+        const int row = used + rest % (kBwdRows - used);
+        rest /= (kBwdRows - used);
+        const int c = rest % L::kChunks;
+        rest /= L::kChunks;
+        const int s = rest & 1;
+        const int which = rest >> 1;  // 0 = Q, 1 = dO
+        const uint32_t a =
+            sbase + (which ? L::kDOOff : L::kQOff) + s * L::kRowBytes + c * L::kRowChunkBytes + row * 128 + unit * 16;
+        st_shared_v4(a, make_uint4(0u, 0u, 0u, 0u));
+      }
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int jb0 = first_block_sh, nblk = nblk_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int nq = 0;
+    bool live = true;
+    if (lane == 0 && nblk > 0) {
+      mbar_arrive_expect_tx(&bar_kv, 2 * L::kKVBytes);
+      for (int c = 0; c < L::kChunks; ++c) {
+        tma_load_4d(sbase + L::kKOff + c * L::kKVChunkBytes, &tmK, &bar_kv, c * 64, g, n0, b);
+        tma_load_4d(sbase + L::kVOff + c * L::kKVChunkBytes, &tmV, &bar_kv, c * 64, g, n0, b);
+      }
+    }
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j & 1;
+      if (j >= 2) {
+        bool okw = true;
+        if (lane == 0) okw = mbar_wait(&bar_qempty[s], ((j - 2) >> 1) & 1, &abort_flag);
+        live = __shfl_sync(0xFFFFFFFFu, okw ? 1 : 0, 0) != 0;
+        if (!live) break;
+      }
+      const int qb = jb0 + j;
+      for (int c = lane; c < kBwdRows; c += 32) {
+        const int qloc = c / p.G;
+        const int qi = qb * p.QTb + qloc;
+        int pos = -1;
+        float lse2 = 0.0f, dl = 0.0f;
+        if (qloc < p.QTb && qi < p.K) {
+          const int hh = g * p.G + (c - qloc * p.G);
+          const int64_t ps = __ldg(p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk);
+          pos = (ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
+          const int64_t ro = static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + hh;
+          lse2 = __ldg(p.lse + ro) * 1.4426950408889634f;
+          dl = __ldg(p.delta + ro);
+        }
+        info_pos[s][c] = pos;
+        info_lse2[s][c] = lse2;
+        info_delta[s][c] = dl;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bar_qfull[s], static_cast<uint32_t>(2 * L::kChunks * p.G * p.QTb * 128));
+        for (int c = 0; c < L::kChunks; ++c) {
+          tma_load_4d(sbase + L::kQOff + s * L::kRowBytes + c * L::kRowChunkBytes, &tmQ, &bar_qfull[s], c * 64,
+                      g * p.G, qb * p.QTb, b);
+          tma_load_4d(sbase + L::kDOOff + s * L::kRowBytes + c * L::kRowChunkBytes, &tmDO, &bar_qfull[s], c * 64,
+                      g * p.G, qb * p.QTb, b);
+        }
+      }
+      ++nq;
+    }
+    if (lane == 0 && nblk > 0) {
+      mbar_wait_drain(&bar_kv, 0);
+      for (int s = 0; s < 2; ++s)
+        if (nq > s) mbar_wait_drain(&bar_qfull[s], ((nq - 1 - s) >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0 && nblk > 0) {
+      constexpr int kAB = kBF16 ? 1 : 0;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBwdKeys, kBwdRows, kAB, false, false);
+      constexpr uint32_t idesc_kv = umma_idesc_f16(kBwdKeys, kBwdHD, kAB, false, true);
+      constexpr uint32_t idesc_q = umma_idesc_f16(kBwdHD, kBwdRows, kAB, true, true);
+      const uint64_t kdesc = sw128_desc(sbase + L::kKOff, 16, 1024);
+      const uint64_t vdesc = sw128_desc(sbase + L::kVOff, 16, 1024);
+      const uint64_t qdesc = sw128_desc(sbase + L::kQOff, 16, 1024);
+      const uint64_t dodesc = sw128_desc(sbase + L::kDOOff, 16, 1024);
+      // the same Q / dO tiles read MN-major (N = hd in 64-column chunks, K = rows)
+      const uint64_t qdesc_mn = sw128_desc(sbase + L::kQOff, L::kRowChunkBytes, 1024);
+      const uint64_t dodesc_mn = sw128_desc(sbase + L::kDOOff, L::kRowChunkBytes, 1024);
+      // K read MN-major as the A of dQ^T (M = hd in 64-column chunks, K = keys)
+      const uint64_t kdesc_mn = sw128_desc(sbase + L::kKOff, L::kKVChunkBytes, 1024);
+      const uint64_t dsdesc = sw128_desc(sbase + L::kDSOff, L::kDSBytes, 1024);
+      bool ok = mbar_wait(&bar_kv, 0, &abort_flag);
+      tc_fence_after();
+      auto issue_rest = [&](int jj) -> bool {
+        const int set = jj & 1;
+        if (!mbar_wait(&bar_pfull[set], (jj >> 1) & 1, &abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t tS = tmem + set * L::kSetCols;
+        const uint64_t rowoff = static_cast<uint64_t>((set * L::kRowBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
+          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
+          umma_ts(tmem + L::kDVCol, tS + kk * 8, dodesc_mn + rowoff + step, idesc_kv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
+          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
+          umma_ts(tmem + L::kDKCol, tS + 32 + kk * 8, qdesc_mn + rowoff + step, idesc_kv,
+                  (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        const uint64_t dsoff = static_cast<uint64_t>((set * L::kDSBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBwdKeys / 16; ++kk) {
+          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
+          umma_ss(tS + 64, kdesc_mn + step, dsdesc + dsoff + step, idesc_q, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar_dqfull[set]);
+        umma_commit(&bar_qempty[set]);
+        return true;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int set = j & 1;
+        if (!mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        // the dQ^T of block j-2 (in this set's dP^T columns) has been read
+        if (j >= 2 && !mbar_wait(&bar_setfree[set], ((j - 2) >> 1) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tS = tmem + set * L::kSetCols;
+        const uint64_t rowoff = static_cast<uint64_t>((set * L::kRowBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBwdHD / 16; ++kk) {
+          const int c = kk >> 2, w = kk & 3;
+          const uint64_t ka = static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4);
+          const uint64_t qa = rowoff + static_cast<uint64_t>((c * L::kRowChunkBytes + w * 32) >> 4);
+          umma_ss(tS, kdesc + ka, qdesc + qa, idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kBwdHD / 16; ++kk) {
+          const int c = kk >> 2, w = kk & 3;
+          const uint64_t va = static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4);
+          const uint64_t da = rowoff + static_cast<uint64_t>((c * L::kRowChunkBytes + w * 32) >> 4);
+          umma_ss(tS + 64, vdesc + va, dodesc + da, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar_sfull[set]);
+        if (j >= 1 && !issue_rest(j - 1)) ok = false;
+      }
+      if (ok) ok = issue_rest(nblk - 1);
+      if (ok) umma_commit(&bar_final);
+      umma_commit(&bar_drain);
+      mbar_wait_drain(&bar_drain, 0);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ P^T, dS^T
+    const int kr = 32 * (warp & 3) + lane;  // key row = TMEM lane
+    const int n = n0 + kr;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const float c2 = p.scale_log2, sc = p.scale;
+    bool ok = nblk > 0;
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int set = j & 1;
+      // the row data of this block (written by the producer before its
+      // arrival) and the S^T / dP^T of this block
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag) &&
+                                       mbar_wait(&bar_sfull[set], (j >> 1) & 1, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tS = tmem + lane_base + set * L::kSetCols;
+      uint32_t sr[2][32], dr[2][32];
+      tmem_ld32(tS, sr[0]);
+      tmem_ld32(tS + 32, sr[1]);
+      tmem_ld32(tS + 64, dr[0]);
+      tmem_ld32(tS + 96, dr[1]);
+      tmem_wait_ld();
+      uint32_t pp[32], dd[32];
+#pragma unroll
+      for (int c = 0; c < kBwdRows; c += 2) {
+        float pv[2], dv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int cc = c + u;
+          const float s = __uint_as_float(sr[cc >> 5][cc & 31]);
+          const float dp = __uint_as_float(dr[cc >> 5][cc & 31]);
+          const float pr = (n <= info_pos[set][cc]) ? fast_exp2(s * c2 - info_lse2[set][cc]) : 0.0f;
+          pv[u] = pr;
+          dv[u] = sc * pr * (dp - info_delta[set][cc]);
+        }
+        pp[c >> 1] = pack2<kBF16>(pv[0], pv[1]);
+        dd[c >> 1] = pack2<kBF16>(dv[0], dv[1]);
+      }
+      tmem_st32(tS, pp);
+      tmem_st32(tS + 32, dd);
+      // dS^T row of this key into the MN-major B tile of dQ^T: 128 bytes,
+      // 16-byte units XOR-swizzled by key % 8
+      const uint32_t rowb = sbase + L::kDSOff + set * L::kDSBytes + kr * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        st_shared_v4(rowb + ((u ^ (kr & 7)) << 4), make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]));
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_pfull[set]);
+    }
+    // ------------------------------------------------------------ dK / dV
+    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_final, 0, &abort_flag));
+    using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+    // the TMEM loads are warp-collective: every lane runs them, only the
+    // stores depend on the lane's key being inside the sequence
+    if (ok || nblk == 0) {
+      tc_fence_after();
+      Elt* dvrow = static_cast<Elt*>(p.dv) + static_cast<int64_t>(b) * p.dv_sb + static_cast<int64_t>(n) * p.dv_ss +
+                   static_cast<int64_t>(g) * p.dv_sh;
+      Elt* dkrow = static_cast<Elt*>(p.dk) + static_cast<int64_t>(b) * p.dk_sb + static_cast<int64_t>(n) * p.dk_ss +
+                   static_cast<int64_t>(g) * p.dk_sh;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        Elt* row = which ? dkrow : dvrow;
+        const uint32_t tcol = tmem + lane_base + (which ? L::kDKCol : L::kDVCol);
+#pragma unroll 1
+        for (int c = 0; c < kBwdHD; c += 32) {
+          uint32_t rr[32];
+          if (nblk > 0) {
+            tmem_ld32(tcol + c, rr);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rr[i] = 0u;
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int col = c + 8 * v;
+            if (n < p.S && col < p.hd) {
+              uint4 w;
+              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]), __uint_as_float(rr[8 * v + 1]));
+              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]), __uint_as_float(rr[8 * v + 3]));
+              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]), __uint_as_float(rr[8 * v + 5]));
+              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]), __uint_as_float(rr[8 * v + 7]));
+              *reinterpret_cast<uint4*>(row + col) = w;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ
+    const int d = 32 * (warp & 3) + lane;  // head-dim column = TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    bool ok = nblk > 0;
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int set = j & 1;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_dqfull[set], (j >> 1) & 1, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      const uint32_t tQ = tmem + lane_base + set * L::kSetCols + 64;
+      tmem_ld32(tQ, r0);
+      tmem_ld32(tQ + 32, r1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_setfree[set]);
+      if (d < p.hd) {
+        const int qb = jb0 + j;
+        const int lim = p.K - qb * p.QTb;  // rows with a query offset below this exist
+        float* base = p.dq + static_cast<int64_t>(b) * p.dq_sb + static_cast<int64_t>(qb) * p.QTb * p.dq_sk + d;
+#pragma unroll
+        for (int c = 0; c < kBwdRows; ++c) {
+          const int ql = row_q[c];
+          if (ql >= 0 && ql < lim) atomicAdd(base + row_off[c], __uint_as_float(c < 32 ? r0[c] : r1[c - 32]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// Delta[b,i,h] = sum_d dO[b,i,h,d] * O[b,i,h,d] in fp32 (one warp per row).
+template <typename T>
+__global__ void __launch_bounds__(256) sqdk_bwd_delta_kernel(const T* __restrict__ o, int64_t o_sb, int64_t o_sk,
+                                                            int64_t o_sh, const T* __restrict__ d_o, int64_t do_sb,
+                                                            int64_t do_sk, int64_t do_sh, float* __restrict__ delta,
+                                                            int B, int K, int H, int hd) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(B) * K * H;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); r < rows;
+       r += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t b = r / (static_cast<int64_t>(K) * H);
+    const int64_t rem = r - b * K * H;
+    const int64_t i = rem / H, h = rem - i * H;
+    const T* orow = o + b * o_sb + i * o_sk + h * o_sh;
+    const T* drow = d_o + b * do_sb + i * do_sk + h * do_sh;
+    float acc = 0.0f;
+    for (int c = lane; c < hd; c += 32) acc = fmaf(static_cast<float>(orow[c]), static_cast<float>(drow[c]), acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+    if (lane == 0) delta[r] = acc;
+  }
+}
+
+// dq (fp32 accumulator, dense [B,K,H,hd]) -> the caller's dtype and strides.
+template <typename T>
+__global__ void __launch_bounds__(256) sqdk_bwd_dq_cast_kernel(const float* __restrict__ acc, T* __restrict__ dq,
+                                                              int64_t sb, int64_t sk, int64_t sh, int B, int K, int H,
+                                                              int hd) {
+  const int64_t n = static_cast<int64_t>(B) * K * H * hd;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * 256) {
+    int64_t rest = e;
+    const int64_t d = rest % hd;
+    rest /= hd;
+    const int64_t h = rest % H;
+    rest /= H;
+    const int64_t i = rest % K;
+    const int64_t b = rest / K;
+    dq[b * sb + i * sk + h * sh + d] = static_cast<T>(acc[e]);
+  }
+}
+
+}  // namespace hspmn

@@ -34,6 +34,13 @@ _SIGNATURES = {
     "hspmn_sqdk_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "hspmn_sqdk_fwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp,
                                       _i64, _i64, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _vp]),
+    "hspmn_sqdk_fwd_lse": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
+                                  _i64, _i64, _i64, _i64, _i64, _i64, _int, ctypes.c_float,
+                                  _vp, ctypes.c_size_t, _vp]),
+    "hspmn_sqdk_bwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
+    "hspmn_sqdk_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                              _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _int,
+                              ctypes.c_float, _vp, ctypes.c_size_t, _vp]),
     "hspmn_rope_gather_rows": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64,
                                       _i64, _i64, _i64, _i64, _i64, _int, _vp]),
     "hspmn_scatter_add_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64,

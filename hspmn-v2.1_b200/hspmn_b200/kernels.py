@@ -4,7 +4,8 @@ Drop-in for ``kernels_v2_1.sparse_query_dense_key_attention``
 (kernels_v2_1.py:141-180): same name, arguments, return convention (a new
 tensor shaped and typed like ``q``) and shape assertions. Grouped K/V heads
 (``k.shape[2] < q.shape[2]``) are supported with the Flex path's semantics
-(hspmn_v2_1.py:212) instead of being indexed as query heads.
+(hspmn_v2_1.py:212) instead of being indexed as query heads. When an input
+requires grad, the result is differentiable (backward on the sm_100a kernels).
 """
 
 from __future__ import annotations
@@ -34,4 +35,7 @@ def sparse_query_dense_key_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
     assert q.shape[-1] == k.shape[-1] == v.shape[-1]
     head_dim = q.shape[-1]
     sm_scale = 1.0 / (head_dim ** 0.5)
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        # the reference's kernel has no backward; this one does (bf16 / f16)
+        return ops.sqdk_attention(q, k, v, q_indices, sm_scale)
     return ops.sqdk_fwd(q, k, v, q_indices, sm_scale)

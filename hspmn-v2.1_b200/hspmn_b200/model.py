@@ -10,9 +10,11 @@ is added into the residual in place (``ops.scatter_add_rows_``); with
 ``sqdk_fused = False`` the reference's order (gather -> SQDK -> zero-filling
 ``ops.scatter_rows`` -> o_proj on all rows) is used. The
 surrounding projections, norms, RoPE and the reflexive stream are stock
-PyTorch, as in the reference. Training mode keeps the reference's
-FlexAttention formulation (hspmn_v2_1.py:200-216), which is outside the
-inference path.
+PyTorch, as in the reference. In training mode the contextual stream of a
+bf16/f16 block on CUDA runs the same attention with its backward on the
+sm_100a kernels (``ops.sqdk_attention``: gather -> SQDK -> scatter, autograd
+through both kernels); with ``sqdk_train = False``, or for float32 blocks, it
+keeps the reference's FlexAttention formulation (hspmn_v2_1.py:200-216).
 """
 
 from __future__ import annotations
@@ -213,6 +215,9 @@ class HSPMNBlock(nn.Module):
         # eval: run q_proj / RoPE / o_proj only on the routed rows (True), or
         # follow the reference's operation order on all rows (False)
         self.sqdk_fused = True
+        # training: SQDK forward + backward kernels for bf16/f16 on CUDA (True),
+        # or the reference's FlexAttention formulation (False)
+        self.sqdk_train = True
         self._init_weights()
 
     def _init_weights(self):
@@ -260,6 +265,28 @@ class HSPMNBlock(nn.Module):
         vec = 16 // x.element_size()
         return self.sqdk_fused and self.head_dim % (2 * vec) == 0
 
+    # -- contextual stream, training: SQDK forward + backward -------------
+    def _sqdk_train_ok(self, q: torch.Tensor, router_out: RouterOutput) -> bool:
+        return (self.sqdk_train and router_out.indices is not None and q.is_cuda
+                and q.dtype in (torch.bfloat16, torch.float16) and self.head_dim % 8 == 0
+                and self.head_dim <= 128 and self.num_heads // self.num_kv_heads <= 64)
+
+    def _attention_sqdk_train(self, q, k, v, router_out: RouterOutput, B: int, S: int, D: int) -> torch.Tensor:
+        """The contextual stream with gradients (the training branch of
+        hspmn_v2_1.py:229-234): the selected query rows are gathered, attend
+        through ``ops.sqdk_attention`` (forward and backward kernels) and are
+        scattered into zero rows before o_proj, which is what the FlexAttention
+        mask (q_idx >= kv_idx) & mask[b, q_idx] computes."""
+        H, hd = self.num_heads, self.head_dim
+        idx = router_out.indices
+        K = idx.shape[1]
+        q_t, k_t, v_t = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        sel = idx[:, :, None, None].expand(B, K, H, hd)
+        q_sel = torch.gather(q_t, 1, sel)
+        attn = ops.sqdk_attention(q_sel, k_t, v_t, idx, 1.0 / math.sqrt(hd))
+        out = torch.zeros_like(q_t).scatter(1, sel, attn)
+        return self.o_proj(out.reshape(B, S, D))
+
     # -- contextual stream, training: reference FlexAttention formulation --
     def _attention_flex(self, q, k, v, router_out: RouterOutput, B: int, S: int, D: int) -> torch.Tensor:
         from torch.nn.attention.flex_attention import create_block_mask
@@ -285,6 +312,8 @@ class HSPMNBlock(nn.Module):
         q, k = apply_rotary_pos_emb(q, k, cos, sin)
         if router_out.indices is not None and not self.training:
             return self._attention_sqdk(q, k, v, router_out, B, S, D)
+        if self._sqdk_train_ok(q, router_out):
+            return self._attention_sqdk_train(q, k, v, router_out, B, S, D)
         return self._attention_flex(q, k, v, router_out, B, S, D)
 
     def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -379,6 +379,29 @@ def _sqdk_operand(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+def _check_sqdk_shapes(name: str, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       indices: torch.Tensor) -> None:
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError(f"{name}: q, k, v must be 4-D ([B,K,H,hd] / [B,S,Hkv,hd])")
+    B, K, H, hd = q.shape
+    Hkv = k.shape[2]
+    if tuple(v.shape) != tuple(k.shape) or k.shape[0] != B or k.shape[3] != hd:
+        raise ValueError(f"{name}: shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if tuple(indices.shape) != (B, K) or indices.dtype != torch.int64:
+        raise ValueError(f"{name}: indices must be int64 [B,K]")
+    if H % Hkv != 0:
+        raise ValueError(f"{name}: num_heads {H} is not a multiple of num_kv_heads {Hkv}")
+
+
+def _sqdk_workspace(dev: torch.device, B: int, K: int, S: int, H: int, Hkv: int, hd: int):
+    with _on_device(dev):
+        ws_bytes = int(N.lib().hspmn_sqdk_workspace_size(B, K, S, H, Hkv, hd))
+    if ws_bytes < 0:
+        raise N.HSPMNNativeError("hspmn_sqdk_workspace_size: device query failed")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    return ws, ws_bytes
+
+
 @torch.library.custom_op("hspmn::sqdk_fwd", mutates_args=())
 def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
              sm_scale: float) -> torch.Tensor:
@@ -389,16 +412,9 @@ def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
     o [B,K,H,hd] in q's dtype. bf16/f16 run natively; float32 operands are
     rounded to bf16 for the tensor cores and the result is returned as float32."""
     dev = _require_cuda(q, k, v, indices)
-    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
-        raise ValueError("sqdk_fwd: q, k, v must be 4-D ([B,K,H,hd] / [B,S,Hkv,hd])")
+    _check_sqdk_shapes("sqdk_fwd", q, k, v, indices)
     B, K, H, hd = q.shape
     S, Hkv = k.shape[1], k.shape[2]
-    if tuple(v.shape) != tuple(k.shape) or k.shape[0] != B or k.shape[3] != hd:
-        raise ValueError(f"sqdk_fwd: shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
-    if tuple(indices.shape) != (B, K) or indices.dtype != torch.int64:
-        raise ValueError("sqdk_fwd: indices must be int64 [B,K]")
-    if H % Hkv != 0:
-        raise ValueError(f"sqdk_fwd: num_heads {H} is not a multiple of num_kv_heads {Hkv}")
     out_dtype = q.dtype
     if q.dtype == torch.float32:
         q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
@@ -406,11 +422,7 @@ def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
         raise TypeError(f"sqdk_fwd: q/k/v dtypes {q.dtype}/{k.dtype}/{v.dtype} unsupported")
     q, k, v = _sqdk_operand(q), _sqdk_operand(k), _sqdk_operand(v)
     o = torch.empty((B, K, H, hd), dtype=q.dtype, device=dev)
-    with _on_device(dev):
-        ws_bytes = int(N.lib().hspmn_sqdk_workspace_size(B, K, S, H, Hkv, hd))
-    if ws_bytes < 0:
-        raise N.HSPMNNativeError("hspmn_sqdk_workspace_size: device query failed")
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    ws, ws_bytes = _sqdk_workspace(dev, B, K, S, H, Hkv, hd)
     with _on_device(dev), _launch("sqdk_fwd", dev):
         rc = N.lib().hspmn_sqdk_fwd(
             ctypes.c_void_p(q.data_ptr()), N.i64_array(q.stride()),
@@ -427,6 +439,121 @@ def sqdk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
 @sqdk_fwd.register_fake
 def _(q, k, v, indices, sm_scale):
     return torch.empty_like(q, memory_format=torch.contiguous_format)
+
+
+# ---------------------------------------------------------------------------
+# SQDK attention, training: forward with log-sum-exp, backward
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("hspmn::sqdk_fwd_lse", mutates_args=())
+def sqdk_fwd_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                 sm_scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``sqdk_fwd`` that also returns each row's log-sum-exp of the scaled
+    scores (float32 [B,K,H], natural log), which ``sqdk_bwd`` needs. q, k, v
+    in bf16 or f16."""
+    dev = _require_cuda(q, k, v, indices)
+    _check_sqdk_shapes("sqdk_fwd_lse", q, k, v, indices)
+    B, K, H, hd = q.shape
+    S, Hkv = k.shape[1], k.shape[2]
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"sqdk_fwd_lse: q/k/v dtypes {q.dtype}/{k.dtype}/{v.dtype} unsupported (bf16 or f16)")
+    o = torch.empty((B, K, H, hd), dtype=q.dtype, device=dev)
+    lse = torch.empty((B, K, H), dtype=torch.float32, device=dev)
+    if B == 0 or K == 0:
+        return o, lse  # no selected query: nothing to attend
+    q, k, v = _sqdk_operand(q), _sqdk_operand(k), _sqdk_operand(v)
+    ws, ws_bytes = _sqdk_workspace(dev, B, K, S, H, Hkv, hd)
+    with _on_device(dev), _launch("sqdk_fwd", dev):
+        rc = N.lib().hspmn_sqdk_fwd_lse(
+            ctypes.c_void_p(q.data_ptr()), N.i64_array(q.stride()),
+            ctypes.c_void_p(k.data_ptr()), N.i64_array(k.stride()),
+            ctypes.c_void_p(v.data_ptr()), N.i64_array(v.stride()),
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0), indices.stride(1),
+            ctypes.c_void_p(o.data_ptr()), N.i64_array(o.stride()),
+            ctypes.c_void_p(lse.data_ptr()), K * H, H,
+            B, K, S, H, Hkv, hd, dtype_code(q.dtype), float(sm_scale),
+            ctypes.c_void_p(ws.data_ptr() if ws is not None else 0), ws_bytes, _stream(dev))
+        N.check(rc, "hspmn_sqdk_fwd_lse")
+    return o, lse
+
+
+@sqdk_fwd_lse.register_fake
+def _(q, k, v, indices, sm_scale):
+    B, K, H, _ = q.shape
+    return torch.empty_like(q, memory_format=torch.contiguous_format), q.new_empty((B, K, H), dtype=torch.float32)
+
+
+@torch.library.custom_op("hspmn::sqdk_bwd", mutates_args=())
+def sqdk_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor, o: torch.Tensor,
+             d_o: torch.Tensor, lse: torch.Tensor,
+             sm_scale: float) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients (dq, dk, dv) of the SQDK attention for the output gradient
+    ``d_o``, given the forward's output ``o`` and ``lse`` (``sqdk_fwd_lse``).
+    The backward of the reference's training path (FlexAttention with the
+    mask (q_idx >= kv_idx) & mask[b, q_idx], hspmn_v2_1.py:200-216)."""
+    dev = _require_cuda(q, k, v, indices, o, d_o, lse)
+    _check_sqdk_shapes("sqdk_bwd", q, k, v, indices)
+    B, K, H, hd = q.shape
+    S, Hkv = k.shape[1], k.shape[2]
+    if not (q.dtype == k.dtype == v.dtype == o.dtype) or q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("sqdk_bwd: q, k, v and o must share one dtype, bf16 or f16")
+    if tuple(o.shape) != tuple(q.shape) or tuple(d_o.shape) != tuple(q.shape) or tuple(lse.shape) != (B, K, H):
+        raise ValueError("sqdk_bwd: o and d_o must be shaped like q, lse [B,K,H]")
+    d_o = d_o.to(q.dtype)
+    q, k, v, o, d_o = (_sqdk_operand(t) for t in (q, k, v, o, d_o))
+    lse = lse.to(torch.float32).contiguous()
+    dq = torch.empty((B, K, H, hd), dtype=q.dtype, device=dev)
+    dk = torch.empty((B, S, Hkv, hd), dtype=q.dtype, device=dev)
+    dv = torch.empty((B, S, Hkv, hd), dtype=q.dtype, device=dev)
+    with _on_device(dev):
+        ws_bytes = int(N.lib().hspmn_sqdk_bwd_workspace_size(B, K, H, hd))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    with _on_device(dev), _launch("sqdk_bwd", dev):
+        rc = N.lib().hspmn_sqdk_bwd(
+            ctypes.c_void_p(q.data_ptr()), N.i64_array(q.stride()),
+            ctypes.c_void_p(k.data_ptr()), N.i64_array(k.stride()),
+            ctypes.c_void_p(v.data_ptr()), N.i64_array(v.stride()),
+            ctypes.c_void_p(indices.data_ptr()), indices.stride(0), indices.stride(1),
+            ctypes.c_void_p(o.data_ptr()), N.i64_array(o.stride()),
+            ctypes.c_void_p(d_o.data_ptr()), N.i64_array(d_o.stride()),
+            ctypes.c_void_p(lse.data_ptr()), K * H, H,
+            ctypes.c_void_p(dq.data_ptr()), N.i64_array(dq.stride()),
+            ctypes.c_void_p(dk.data_ptr()), N.i64_array(dk.stride()),
+            ctypes.c_void_p(dv.data_ptr()), N.i64_array(dv.stride()),
+            B, K, S, H, Hkv, hd, dtype_code(q.dtype), float(sm_scale),
+            ctypes.c_void_p(ws.data_ptr() if ws is not None else 0), ws_bytes, _stream(dev))
+        N.check(rc, "hspmn_sqdk_bwd")
+    return dq, dk, dv
+
+
+@sqdk_bwd.register_fake
+def _(q, k, v, indices, o, d_o, lse, sm_scale):
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            torch.empty_like(k, memory_format=torch.contiguous_format),
+            torch.empty_like(v, memory_format=torch.contiguous_format))
+
+
+class _SqdkAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, indices, sm_scale):
+        o, lse = sqdk_fwd_lse(q, k, v, indices, sm_scale)
+        ctx.save_for_backward(q, k, v, indices, o, lse)
+        ctx.sm_scale = sm_scale
+        return o
+
+    @staticmethod
+    def backward(ctx, d_o):
+        q, k, v, indices, o, lse = ctx.saved_tensors
+        dq, dk, dv = sqdk_bwd(q, k, v, indices, o, d_o, lse, ctx.sm_scale)
+        return dq, dk, dv, None, None
+
+
+def sqdk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                   sm_scale: float) -> torch.Tensor:
+    """Differentiable SQDK attention: ``sqdk_fwd_lse`` forward, ``sqdk_bwd``
+    backward (bf16 / f16 operands)."""
+    return _SqdkAttention.apply(q, k, v, indices, sm_scale)
 
 
 def device_errors(device: Optional[torch.device] = None, clear: bool = True) -> int:

@@ -5,6 +5,8 @@
  *   (fp32 gate ->) router top-K  ->  gather selected queries  ->  SQDK causal attention
  *                 ->  scatter back into the [B,S,D] stream
  *
+ * and, for training, the backward of the SQDK attention.
+ *
  * Conventions
  *   - All buffers are device memory allocated by the caller; the library never
  *     allocates and never synchronises the stream it is given.
@@ -227,6 +229,54 @@ HSPMN_API int hspmn_sqdk_fwd_noalloc(const void* q, const int64_t* q_strides,
                    void* o, const int64_t* o_strides,
                    int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
                    int64_t hd, int dtype, float sm_scale, void* stream);
+
+/*
+ * hspmn_sqdk_fwd that also writes each row's log-sum-exp of the scaled scores
+ * (natural log) to lse[b*lse_sb + i*lse_sk + h] (float32; lse_sk >= H), the
+ * statistic hspmn_sqdk_bwd needs. Other arguments, results and errors as
+ * hspmn_sqdk_fwd.
+ */
+HSPMN_API int hspmn_sqdk_fwd_lse(const void* q, const int64_t* q_strides,
+                   const void* k, const int64_t* k_strides,
+                   const void* v, const int64_t* v_strides,
+                   const int64_t* idx, int64_t idx_sb, int64_t idx_sk,
+                   void* o, const int64_t* o_strides,
+                   float* lse, int64_t lse_sb, int64_t lse_sk,
+                   int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
+                   int64_t hd, int dtype, float sm_scale,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of device workspace hspmn_sqdk_bwd needs (0 when K == 0). */
+HSPMN_API int64_t hspmn_sqdk_bwd_workspace_size(int64_t B, int64_t K, int64_t H, int64_t hd);
+
+/*
+ * Backward of the SQDK attention. Replaces the gradient the reference's
+ * training path takes through FlexAttention (hspmn_v2_1.py:200-216: mask
+ * (q_idx >= kv_idx) & mask[b, q_idx] with enable_gqa, which is this
+ * attention over the selected rows):
+ *   dq = dL/dq [B,K,H,hd], dk = dL/dk and dv = dL/dv [B,S,Hkv,hd]
+ * for the output gradient d_o [B,K,H,hd], given the forward's inputs, its
+ * output o and its lse (from hspmn_sqdk_fwd_lse, dense [B,K,H]: lse_sb = K*H,
+ * lse_sk = H). All tensors of `dtype` (bf16 or f16) with the last dimension
+ * contiguous; q, k, v, d_o, dk, dv 16-byte aligned with 16-byte strides.
+ * dk and dv are written in full (zero where no selected query sees a key).
+ * workspace: hspmn_sqdk_bwd_workspace_size() bytes (16-byte aligned; holds
+ * rowsum(dO * O) and an fp32 dq accumulator). hd: multiple of 8, <= 128;
+ * H / Hkv <= 64. With K == 0 the query-side pointers may be null.
+ */
+HSPMN_API int hspmn_sqdk_bwd(const void* q, const int64_t* q_strides,
+                   const void* k, const int64_t* k_strides,
+                   const void* v, const int64_t* v_strides,
+                   const int64_t* idx, int64_t idx_sb, int64_t idx_sk,
+                   const void* o, const int64_t* o_strides,
+                   const void* d_o, const int64_t* do_strides,
+                   const float* lse, int64_t lse_sb, int64_t lse_sk,
+                   void* dq, const int64_t* dq_strides,
+                   void* dk, const int64_t* dk_strides,
+                   void* dv, const int64_t* dv_strides,
+                   int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv,
+                   int64_t hd, int dtype, float sm_scale,
+                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Read (and optionally clear) the current device's HSPMN_DEVERR_* flag word.

@@ -98,6 +98,31 @@ def test_gate_validation():
     assert gate(B=0) == 0                                     # empty: nothing to do
 
 
+def test_sqdk_backward_validation():
+    lib = N.lib()
+    p = ctypes.c_void_p(4096)
+    B, K, S, H, Hkv, hd = 1, 16, 256, 8, 2, 64
+    qs = (ctypes.c_int64 * 4)(K * H * hd, H * hd, hd, 1)
+    ks = (ctypes.c_int64 * 4)(S * Hkv * hd, Hkv * hd, hd, 1)
+
+    def bwd(k=p, dk=p, q=p, dtype=2, hd_=hd, H_=H, Hkv_=Hkv, K_=K, lse_sb=K * H, ws=p, ws_bytes=1 << 20):
+        return lib.hspmn_sqdk_bwd(q, qs, k, ks, k, ks, p, K_, 1, p, qs, p, qs, p, lse_sb, H_, p, qs, dk, ks, dk, ks,
+                                  B, K_, S, H_, Hkv_, hd_, dtype, 0.125, ws, ws_bytes, None)
+
+    assert bwd(k=None) == -1 and bwd(dk=None) == -1 and bwd(q=None) == -1
+    assert bwd(dtype=0) == -2                      # f32 operands are not supported
+    assert bwd(hd_=12) == -4 and bwd(hd_=136) == -4
+    assert bwd(H_=6, Hkv_=4) == -4                 # heads not a multiple of kv heads
+    assert bwd(lse_sb=K * H + 1) == -1             # lse must be dense [B,K,H]
+    assert bwd(ws=None) == -1 and bwd(ws_bytes=16) == -1
+    assert bwd(k=ctypes.c_void_p(4100)) == -3
+    assert lib.hspmn_sqdk_bwd_workspace_size(1, 16, 8, 64) == 512 + 16 * 8 * 64 * 4
+    assert lib.hspmn_sqdk_bwd_workspace_size(1, 0, 8, 64) == 0
+    # the forward with log-sum-exp needs somewhere to put it
+    assert lib.hspmn_sqdk_fwd_lse(p, qs, p, ks, p, ks, p, K, 1, p, qs, None, K * H, H, B, K, S, H, Hkv, hd, 2,
+                                  0.125, None, 0, None) == -1
+
+
 def test_rope_and_scatter_add_validation():
     lib = N.lib()
     p = ctypes.c_void_p(4096)

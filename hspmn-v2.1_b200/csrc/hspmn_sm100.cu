@@ -93,7 +93,8 @@ EncodeTiledFn encode_fn() {
 // 4-D tiled map over a [d3][d2][d1][d0] tensor (d0 innermost, stride 1),
 // 128-byte swizzle, zero fill out of bounds. Strides in bytes.
 int encode_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[4],
-              const uint64_t strides_bytes[3], const uint32_t box[4]) {
+              const uint64_t strides_bytes[3], const uint32_t box[4],
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return HSPMN_ERR_CUDA;
   cuuint64_t gd[4] = {dims[0], dims[1], dims[2], dims[3]};
@@ -101,7 +102,7 @@ int encode_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const 
   cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
   cuuint32_t es[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, dt, 4, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? HSPMN_OK : HSPMN_ERR_INVALID;
 }
@@ -637,6 +638,18 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
     if (int rc = encode_4d(&mk, k, dt, dims, sk, box)) return rc;
     if (int rc = encode_4d(&mv, v, dt, dims, sv, box)) return rc;
   }
+  // the fp32 dq accumulator, added into per query block with bulk tensor reduces
+  CUtensorMap mdq;
+  std::memset(&mdq, 0, sizeof(mdq));
+  if (K > 0) {
+    const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(H), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(B)};
+    const uint64_t sq[3] = {static_cast<uint64_t>(hd * 4), static_cast<uint64_t>(H * hd * 4),
+                            static_cast<uint64_t>(K * H * hd * 4)};
+    const uint32_t box[4] = {64u, static_cast<uint32_t>(G), static_cast<uint32_t>(QTb), 1u};
+    if (int rc = encode_4d(&mdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dims, sq, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  }
   SqdkBwdParams prm;
   prm.idx = idx;
   prm.idx_sb = idx_sb;
@@ -646,9 +659,6 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
   prm.row_sb = K * H;
   prm.row_sk = H;
   prm.dq = dq_acc;
-  prm.dq_sb = K * H * hd;
-  prm.dq_sk = H * hd;
-  prm.dq_sh = hd;
   prm.dk = dk;
   prm.dv = dv;
   prm.dk_sb = dks[0];
@@ -673,7 +683,7 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
   auto kern = dtype == HSPMN_BF16 ? sqdk_bwd_kernel<true> : sqdk_bwd_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SqdkBwdLayout::kAlloc) != cudaSuccess)
     return HSPMN_ERR_CUDA;
-  kern<<<static_cast<unsigned>(grid), kBwdThreads, SqdkBwdLayout::kAlloc, st>>>(mq, mk, mv, mdo, prm);
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, SqdkBwdLayout::kAlloc, st>>>(mq, mk, mv, mdo, mdq, prm);
   if (int rc = launch_status()) return rc;
   if (K > 0) {
     const int64_t n = B * K * H * hd;

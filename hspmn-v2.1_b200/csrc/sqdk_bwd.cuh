@@ -17,8 +17,10 @@
 //   dV  += P^T dO      tcgen05.mma TS (A = P^T in TMEM, B = dO MN-major)
 //   dK  += dS^T Q      tcgen05.mma TS (A = dS^T in TMEM, B = Q MN-major)
 //   dQ^T = K^T dS      tcgen05.mma SS (A = K MN-major, B = dS MN-major), into
-//                      the columns dP^T used; added into an fp32 dQ in global
-//                      memory (other key blocks add to the same rows)
+//                      the columns dP^T used; staged in shared memory and added
+//                      into an fp32 dQ in global memory with one bulk tensor
+//                      reduce per 64 columns (other key blocks add to the same
+//                      rows)
 // dK and dV accumulate in TMEM over all query blocks and are stored once.
 //
 // TMEM (512 columns, one CTA per SM): two sets of [S^T | dP^T] (64 + 64
@@ -30,7 +32,8 @@
 //               ring; writes each block's per-row data (position, lse, Delta)
 //   warp 1      TMEM allocation + single-thread MMA issue
 //   warps 2..5  P^T / dS^T (thread = key), then the dK / dV epilogue
-//   warps 6..9  dQ: TMEM -> registers -> fp32 reductions (thread = column d)
+//   warps 6..9  dQ: TMEM -> registers -> shared staging (thread = column d),
+//               then one thread issues the bulk reduces into global dQ
 // Every mbarrier wait is bounded; a wait that gives up flags
 // HSPMN_DEVERR_TIMEOUT, the other roles stop, and the CTA drains its copies
 // and MMAs and frees its tensor memory before returning. TMEM loads and
@@ -47,6 +50,7 @@ constexpr int kBwdKeys = 128;   // keys per CTA (M of the key-major products)
 constexpr int kBwdRows = 64;    // rows (query, head) per query block
 constexpr int kBwdThreads = 320;
 constexpr int kBwdHD = 128;     // head_dim tile (hd <= 128; columns past hd are zero)
+constexpr int kBwdDQBar = 1;    // named barrier of the four dQ warps
 
 struct SqdkBwdLayout {
   static constexpr int kChunks = kBwdHD / 64;
@@ -60,7 +64,9 @@ struct SqdkBwdLayout {
   static constexpr int kQOff = kVOff + kKVBytes;
   static constexpr int kDOOff = kQOff + 2 * kRowBytes;
   static constexpr int kDSOff = kDOOff + 2 * kRowBytes;
-  static constexpr int kBytes = kDSOff + 2 * kDSBytes;
+  static constexpr int kDQChunkBytes = kBwdRows * 64 * 4;  // 64 rows x 64 fp32 columns, row-major
+  static constexpr int kDQOff = kDSOff + 2 * kDSBytes;
+  static constexpr int kBytes = kDQOff + kChunks * kDQChunkBytes;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kSetCols = 128;  // S^T at +0, dP^T / dQ^T at +64
@@ -74,8 +80,7 @@ struct SqdkBwdParams {
   const float* lse;    // [B,K,H] natural-log log-sum-exp from the forward
   const float* delta;  // [B,K,H] rowsum(dO * O)
   int64_t row_sb, row_sk;  // strides of lse / delta (elements; head stride 1)
-  float* dq;           // fp32 [B,K,H,hd] accumulator (zeroed by the host)
-  int64_t dq_sb, dq_sk, dq_sh;
+  float* dq;           // fp32 [B,K,H,hd] accumulator (zeroed by the host; written through tmDQ)
   void* dk;
   void* dv;
   int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
@@ -97,7 +102,7 @@ template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     sqdk_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const SqdkBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const SqdkBwdParams p) {
   using L = SqdkBwdLayout;
   extern __shared__ uint8_t sqdk_bwd_smem_raw[];
   __shared__ __align__(8) uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_pfull[2];
@@ -106,7 +111,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __shared__ int first_block_sh, nblk_sh;
   __shared__ int info_pos[2][kBwdRows];
   __shared__ float info_lse2[2][kBwdRows], info_delta[2][kBwdRows];
-  __shared__ int row_q[kBwdRows], row_off[kBwdRows];  // per row: query offset in the block (-1: none), dq offset
   __shared__ volatile uint32_t abort_flag;
 
   const uint32_t sbase = (smem_u32(sqdk_bwd_smem_raw) + 1023u) & ~1023u;
@@ -144,11 +148,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, L::kTmemCols);
     tmem_relinquish();
-  }
-  if (threadIdx.x < kBwdRows) {
-    const int c = threadIdx.x, qloc = c / p.G;
-    row_q[c] = qloc < p.QTb ? qloc : -1;
-    row_off[c] = static_cast<int>(qloc * p.dq_sk + (g * p.G + c - qloc * p.G) * p.dq_sh);
   }
   // rows of the query tiles past G * QTb are never written by TMA: zero them
   // once, so the row sums of dV / dK see exact zeros there
@@ -412,7 +411,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = nblk > 0;
     for (int j = 0; ok && j < nblk; ++j) {
       const int set = j & 1;
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_dqfull[set], (j >> 1) & 1, &abort_flag));
+      // the four dQ warps agree on the wait's outcome, so all of them take the
+      // named barriers below the same number of times
+      ok = named_bar_and(kBwdDQBar, 128, mbar_wait(&bar_dqfull[set], (j >> 1) & 1, &abort_flag));
       if (!ok) break;
       tc_fence_after();
       uint32_t r0[32], r1[32];
@@ -423,17 +424,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_setfree[set]);
-      if (d < p.hd) {
-        const int qb = jb0 + j;
-        const int lim = p.K - qb * p.QTb;  // rows with a query offset below this exist
-        float* base = p.dq + static_cast<int64_t>(b) * p.dq_sb + static_cast<int64_t>(qb) * p.QTb * p.dq_sk + d;
+      // the previous block's reduces have read the staging tile
+      if (warp == 6 && lane == 0) tma_store_wait_read();
+      named_bar_sync(kBwdDQBar, 128);
+      // dQ^T column d of the 64 rows -> row-major staging, one 64-column chunk
+      // per TMA box (a warp writes 32 consecutive floats of a row at a time)
+      const uint32_t col = sbase + L::kDQOff + (d >> 6) * L::kDQChunkBytes + (d & 63) * 4;
 #pragma unroll
-        for (int c = 0; c < kBwdRows; ++c) {
-          const int ql = row_q[c];
-          if (ql >= 0 && ql < lim) atomicAdd(base + row_off[c], __uint_as_float(c < 32 ? r0[c] : r1[c - 32]));
-        }
+      for (int c = 0; c < 32; ++c) {
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + c * 256), "r"(r0[c]) : "memory");
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + (c + 32) * 256), "r"(r1[c]) : "memory");
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(kBwdDQBar, 128);
+      if (warp == 6 && lane == 0) {
+        // rows past the K selected queries are clipped by the tensor map
+        const int qb = jb0 + j;
+        for (int ch = 0; ch < L::kChunks && ch * 64 < p.hd; ++ch)
+          tma_reduce_add_4d(&tmDQ, sbase + L::kDQOff + ch * L::kDQChunkBytes, ch * 64, g * p.G, qb * p.QTb, b);
+        tma_store_commit();
       }
     }
+    if (warp == 6 && lane == 0) tma_store_wait_read();
   }
 
   tc_fence_before();

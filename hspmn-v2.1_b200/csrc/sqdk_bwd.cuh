@@ -51,6 +51,7 @@ constexpr int kBwdRows = 64;    // rows (query, head) per query block
 constexpr int kBwdThreads = 320;
 constexpr int kBwdHD = 128;     // head_dim tile (hd <= 128; columns past hd are zero)
 constexpr int kBwdDQBar = 1;    // named barrier of the four dQ warps
+static_assert(kBwdRows == 64, "the producer writes two rows of block data per lane");
 
 struct SqdkBwdLayout {
   static constexpr int kChunks = kBwdHD / 64;
@@ -189,29 +190,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int j = 0; j < nblk; ++j) {
       const int s = j & 1;
+      const int qb = jb0 + j;
+      // this block's row data (two rows per lane), loaded before waiting for
+      // the stage: the loads do not touch it, so their latency overlaps the wait
+      int pos[2];
+      float lse2[2], dl[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = lane + 32 * u;
+        const int qloc = c / p.G;
+        const int qi = qb * p.QTb + qloc;
+        pos[u] = -1;
+        lse2[u] = 0.0f;
+        dl[u] = 0.0f;
+        if (qloc < p.QTb && qi < p.K) {
+          const int hh = g * p.G + (c - qloc * p.G);
+          const int64_t ps = __ldg(p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk);
+          pos[u] = (ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
+          const int64_t ro = static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + hh;
+          lse2[u] = __ldg(p.lse + ro) * 1.4426950408889634f;
+          dl[u] = __ldg(p.delta + ro);
+        }
+      }
       if (j >= 2) {
         bool okw = true;
         if (lane == 0) okw = mbar_wait(&bar_qempty[s], ((j - 2) >> 1) & 1, &abort_flag);
         live = __shfl_sync(0xFFFFFFFFu, okw ? 1 : 0, 0) != 0;
         if (!live) break;
       }
-      const int qb = jb0 + j;
-      for (int c = lane; c < kBwdRows; c += 32) {
-        const int qloc = c / p.G;
-        const int qi = qb * p.QTb + qloc;
-        int pos = -1;
-        float lse2 = 0.0f, dl = 0.0f;
-        if (qloc < p.QTb && qi < p.K) {
-          const int hh = g * p.G + (c - qloc * p.G);
-          const int64_t ps = __ldg(p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk);
-          pos = (ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
-          const int64_t ro = static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + hh;
-          lse2 = __ldg(p.lse + ro) * 1.4426950408889634f;
-          dl = __ldg(p.delta + ro);
-        }
-        info_pos[s][c] = pos;
-        info_lse2[s][c] = lse2;
-        info_delta[s][c] = dl;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = lane + 32 * u;
+        info_pos[s][c] = pos[u];
+        info_lse2[s][c] = lse2[u];
+        info_delta[s][c] = dl[u];
       }
       __syncwarp();
       if (lane == 0) {

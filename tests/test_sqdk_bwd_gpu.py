@@ -158,3 +158,20 @@ def test_block_training_step_matches_dense_attention():
         a, r = g_sqdk[n], g_ref[n]
         rel = (a - r).norm() / r.norm().clamp_min(1e-30)
         assert rel <= 3e-2, (n, float(rel))
+
+
+def test_lse_and_grads_on_a_launch_without_key_splits():
+    """Enough tiles (16 sequences x 820 rows, H=16, Hkv=4) that the forward
+    runs unsplit, so its own epilogue writes the log-sum-exp; sequences 0
+    and 15 are checked against the oracle, lse and gradients."""
+    B, S, H, Hkv, hd, K = 16, 4096, 16, 4, 128, 820
+    q, k, v, d_o, idx = _inputs(B, S, H, Hkv, hd, K, seed=77)
+    o, lse, dq, dk, dv = _run(q, k, v, d_o, idx)
+    for b in (0, B - 1):
+        sl = slice(b, b + 1)
+        qf, kf, vf, dof = (t[sl].float().numpy() for t in (q, k, v, d_o))
+        rdq, rdk, rdv, rlse = oracle.sqdk_bwd_fp32(qf, kf, vf, idx[sl].numpy(), dof)
+        assert np.abs(lse[sl].cpu().numpy() - rlse).max() <= 1e-5
+        _close("dq", dq[sl], rdq)
+        _close("dk", dk[sl], rdk)
+        _close("dv", dv[sl], rdv)

@@ -7,26 +7,38 @@ dim=2048, num_heads=16, num_kv_heads=4 (the config default), k=0.2, S=4096,
 one block forward over the GPU's batch; the router top-K, the row gathers
 (with the query RoPE fused), SQDK attention and the residual write-back of
 the routed rows inside it are this library's sm_100a kernels; the
-projections (cuBLAS), norms, K RoPE and the reflexive stream are stock
-PyTorch. Multi-GPU: one process per GPU (torchrun), every rank runs its
-own 64 sequences with replicated weights and no data-path collective (weak
+projections (cuBLAS), norms and the reflexive stream are stock PyTorch.
+Multi-GPU: one process per GPU (torchrun), every rank runs its own 64
+sequences with replicated weights and no data-path collective (weak
 scaling); the timed region is bracketed by barriers and the max over ranks is
 reported.
+
+After the timed block steps the same run adds, untimed unless stated:
+  * ``headline_parity``: two sequences of the timed B=64 SQDK launch against
+    the fp32 oracle;
+  * ``long_parity``: the sequence-sharded block over all ranks at S=32768
+    against the plain one-GPU block forward on rank 0;
+  * ``long_context``: the S=262144 single sequence sequence-sharded over all
+    ranks (strong scaling), timed, with the K/V exchange timed on its own;
+  * at N=1: the standalone sparsity sweep (B=8, S=32768, H=Hkv=16, hd=128,
+    k in {0.05, 0.1, 0.2, 0.5}) and library GPU comparators of the SQDK
+    attention (torch SDPA with a boolean mask, and the reference's own
+    dense-masked PyTorch SQDK pattern run on the GPU);
+  * at N=1: ``cpu_baseline``, the reference's PyTorch CPU path (a torch
+    restatement of HSPMNBlock.forward with eager FlexAttention, as the
+    reference runs without a GPU) on all host cores.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload block|sqdk-sweep|sqdk|sqdk-bwd|long]
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-numpy oracle port of HSPMNBlock.forward) on the host cores, one sequence of
-the same workload per step; under torchrun only rank 0 runs it.
-``--workload sqdk-sweep`` runs the standalone router / gather / SQDK / scatter
-sweep (B=8, S=32768, H=Hkv=16, hd=128, k in {0.05, 0.1, 0.2, 0.5}) and
-prints one line per k; ``--workload sqdk`` runs the same standalone path at
-``--batch/--seq-len/--heads/--kv-heads/--sparsity``. ``--workload long`` runs
-one sequence of ``--seq-len`` tokens (262144 for the long-context
-configuration) sequence-sharded over the ranks (strong scaling).
-``--workload sqdk-bwd`` times the SQDK backward (the training path's
-attention gradients) at the block's attention shape.
+``--impl reference`` times the reference's CPU path (the torch restatement
+above) on all host cores, one sequence of the block workload per step; under
+torchrun only rank 0 runs it. ``--workload sqdk-sweep`` prints the sweep as
+one line per k; ``--workload sqdk`` runs the same standalone path at
+``--batch/--seq-len/--heads/--kv-heads/--sparsity``; ``--workload long`` runs
+only the long-context measurement; ``--workload sqdk-bwd`` times the SQDK
+backward (the training path's attention gradients) at the block's attention
+shape.
 """
 
 from __future__ import annotations
@@ -50,6 +62,8 @@ for _p in (os.path.join(REPO, "hspmn-v2.1_b200"), REPO):
 METRIC = "SQDK block tok/s at B=64,S=4096,D=2048,k=0.2; attention TFLOPS % of bf16 peak"
 PUBLISHED_TOK_S = 1406304.0  # reference README.md:30, RTX 5090, same block config
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+LONG_SEQ = 262144
+LONG_PARITY_SEQ = 32768
 
 
 def parse_args():
@@ -66,7 +80,10 @@ def parse_args():
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--sparsity", type=float, default=0.2)
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--long-steps", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="only the timed block steps (no parity, long-context, sweep, comparators)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     a = ap.parse_args()
@@ -161,57 +178,136 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle port of the reference algorithm on host cores
+# CPU side: the reference's PyTorch CPU path, and the numpy oracle port
 # ---------------------------------------------------------------------------
 
 
-def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = max((d.get("num_threads", 1) for d in threadpool_info()), default=1)
-        return int(n)
-    except Exception:  # pragma: no cover
-        return os.cpu_count() or 1
-
-
-def cpu_block_sample(args, seconds: float, max_steps: int | None = None, warmup: int = 1):
-    """Time the numpy oracle's HSPMNBlock forward on one sequence of the
-    workload. Returns (tok/s, sample description, cores, per-step seconds)."""
-    import numpy as np
+def use_all_host_cores() -> int:
+    """torch and the BLAS pools on every host core, whatever OMP_NUM_THREADS
+    a launcher set (torchrun sets 1). Returns the thread count in use."""
     import torch
 
-    import oracle
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except Exception:  # pragma: no cover
+        pass
+    return n
+
+
+def _cpu_block_setup(args):
+    import torch
+
     from hspmn_b200 import HSPMNBlock, HSPMNConfig, seed_everything
 
     seed_everything(42)
     cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads,
                       sparsity_k=args.sparsity, max_seq_len=args.seq_len)
     block = HSPMNBlock(cfg).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(1000)
+    x = torch.randn(1, args.seq_len, args.dim, generator=g).to(torch.bfloat16)
+    return cfg, block, x
+
+
+def cpu_reference_sample(args, steps: int | None = None, seconds: float = 0.0, warmup: int = 3):
+    """Time the reference's PyTorch CPU path (oracle.torch_cpu_ref: the
+    reference HSPMNBlock.forward with eager FlexAttention, its path without a
+    GPU) on one sequence of the block workload, on all host cores. The first
+    two warm-up steps run the module in float32 and in bfloat16; the faster
+    dtype is timed. Returns a dict with tok/s, ms/step, dtype, cores and the
+    sample description."""
+    import warnings
+
+    import torch
+
+    from oracle.torch_cpu_ref import block_forward_torch
+
+    warnings.filterwarnings("ignore", message=".*flex_attention called without torch.compile.*")
+    cores = use_all_host_cores()
+    cfg, block, x_bf16 = _cpu_block_setup(args)
+    sds = {dt: {k: v.to(dt) for k, v in block.state_dict().items()} for dt in (torch.float32, torch.bfloat16)}
+    xs = {dt: x_bf16.to(dt) for dt in sds}
+
+    def step(dt):
+        t0 = time.perf_counter()
+        block_forward_torch(sds[dt], xs[dt], args.heads, args.kv_heads, cfg.rope_base, cfg.block_size)
+        return time.perf_counter() - t0
+
+    step(torch.float32)  # first call builds the block mask machinery
+    probe = {dt: step(dt) for dt in sds}
+    dt = min(probe, key=probe.get)
+    for _ in range(max(0, warmup - 2)):
+        step(dt)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        times.append(step(dt))
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start >= seconds:
+            break
+    per = statistics.mean(times)
+    name = str(dt).replace("torch.", "")
+    return {"value": args.seq_len / per, "unit": "tok/s", "cores": cores, "kind": "port",
+            "dtype": name, "ms_per_step": per * 1e3,
+            "sample": (f"reference HSPMNBlock.forward on its CPU path (eager FlexAttention: dense S x S attention), "
+                       f"torch restatement pinned to the reference's block outputs, {name} (faster of f32/bf16 "
+                       f"on this host: f32 {probe[torch.float32]:.2f} s, bf16 {probe[torch.bfloat16]:.2f} s), "
+                       f"one sequence S={args.seq_len} D={args.dim} per step, {len(times)} timed step(s), "
+                       f"{cores} threads")}
+
+
+def cpu_oracle_sample(args, seconds: float):
+    """Time the numpy oracle's HSPMNBlock forward (sparse attention over the
+    selected rows only) on one sequence of the workload."""
+    import oracle
+
+    cores = use_all_host_cores()
+    cfg, block, x = _cpu_block_setup(args)
     params = {k: v.float().numpy() for k, v in block.state_dict().items()}
     ts = float(block.router.target_sparsity.item())
-    g = torch.Generator().manual_seed(1000)
-    x = torch.randn(1, args.seq_len, args.dim, generator=g).to(torch.bfloat16).float().numpy()
-    eps = float(torch.finfo(torch.bfloat16).eps)
+    xn = x.float().numpy()
+    eps = 0.0078125  # finfo(bfloat16).eps, the module dtype's
 
     def step():
-        oracle.block_forward(params, x, args.heads, args.kv_heads, ts, cfg.rope_base, eps, noisy_dtype="bf16")
+        oracle.block_forward(params, xn, args.heads, args.kv_heads, ts, cfg.rope_base, eps, noisy_dtype="bf16")
 
-    for _ in range(warmup):
-        step()
+    step()
     times = []
     t_start = time.perf_counter()
     while True:
         t0 = time.perf_counter()
         step()
         times.append(time.perf_counter() - t0)
-        if max_steps is not None and len(times) >= max_steps:
-            break
-        if max_steps is None and time.perf_counter() - t_start >= seconds:
+        if time.perf_counter() - t_start >= seconds:
             break
     per = statistics.mean(times)
-    sample = (f"numpy oracle HSPMNBlock.forward (fp32 arithmetic on bf16-valued weights/inputs), one sequence "
-              f"S={args.seq_len} D={args.dim} per step, {len(times)} timed step(s) after {warmup} warm-up")
-    return args.seq_len / per, sample, cpu_threads(), per
+    return {"value": args.seq_len / per, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": (f"numpy oracle HSPMNBlock.forward (attention over the selected rows only, fp32), one "
+                       f"sequence S={args.seq_len} D={args.dim} per step, {len(times)} timed step(s)")}
+
+
+def cpu_sqdk_cfg1(iters: int = 200):
+    """The reference's PyTorch SQDK test pattern (test_kernels_v2_1.py:34-65)
+    in fp32 at B=2, S=512, H=4, hd=64, K=102 on the host cores: ms per call."""
+    import torch
+
+    from oracle.torch_cpu_ref import sqdk_dense_torch
+
+    cores = use_all_host_cores()
+    g = torch.Generator().manual_seed(42)
+    B, S, H, hd, K = 2, 512, 4, 64, 102
+    q, k, v = (torch.randn(B, S, H, hd, generator=g) for _ in range(3))
+    idx = torch.stack([torch.sort(torch.randperm(S, generator=g)[:K])[0] for _ in range(B)])
+    for _ in range(5):
+        sqdk_dense_torch(q, k, v, idx)
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        sqdk_dense_torch(q, k, v, idx)
+    return {"ms_per_call": (time.perf_counter() - t0) / iters * 1e3, "cores": cores,
+            "sample": f"B={B} S={S} H={H} hd={hd} K={K} fp32, {iters} calls"}
 
 
 def run_reference(args):
@@ -219,21 +315,21 @@ def run_reference(args):
     if rank != 0:
         return
     steps = max(1, args.steps)
-    tok_s, sample, cores, per = cpu_block_sample(args, 0.0, max_steps=steps, warmup=min(args.warmup, 1))
+    ref = cpu_reference_sample(args, steps=steps, warmup=args.warmup)
     line = {
-        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": tok_s / PUBLISHED_TOK_S, "dtype": "f32",
+        "impl": "reference", "metric": METRIC, "value": ref["value"], "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ref["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": ref["value"] / PUBLISHED_TOK_S, "dtype": ref["dtype"],
         "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
         "config": workload_config(args),
-        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": ref,
+        "e2e": {"value": ref["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
-# our arm
+# distributed helpers
 # ---------------------------------------------------------------------------
 
 
@@ -249,15 +345,24 @@ def workload_config(args, per_gpu_batch=None):
     }
 
 
-def init_dist(world, local_rank):
+def init_dist(world, local_rank, always_group=False):
+    """CUDA device of this rank; an NCCL process group when world > 1 (or,
+    with ``always_group``, a one-rank group so the collective code path is
+    the same at N=1)."""
     import torch
     import torch.distributed as dist
 
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-    return torch.device("cuda", local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1 or always_group:
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 2000)))
+            dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=300),
+                                    device_id=dev)
+        else:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    return dev
 
 
 def barrier(world):
@@ -281,13 +386,316 @@ def max_over_ranks(val: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def free_cuda():
+    import gc
+
+    import torch
+
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+# ---------------------------------------------------------------------------
+# parity of the timed headline launch
+# ---------------------------------------------------------------------------
+
+
+def headline_parity(model, x):
+    """Run one block forward with the SQDK call captured, then compare the
+    first and last sequence of that (timed-shape) launch against the fp32
+    oracle on the same inputs."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from hspmn_b200 import ops
+
+    captured = {}
+    real = ops.sqdk_fwd
+
+    def capture(q, k, v, idx, scale):
+        o = real(q, k, v, idx, scale)
+        captured.update(q=q, k=k, v=v, idx=idx, o=o, scale=scale)
+        return o
+
+    ops.sqdk_fwd = capture
+    try:
+        with torch.no_grad():
+            model(x)
+        torch.cuda.synchronize()
+    finally:
+        ops.sqdk_fwd = real
+    B = captured["q"].shape[0]
+    res = {"launch_batch": B, "sequences": [0, B - 1]}
+    worst_max, worst_mean = 0.0, 0.0
+    for b in (0, B - 1):
+        q = captured["q"][b:b + 1].float().cpu().numpy()
+        k = captured["k"][b:b + 1].float().cpu().numpy()
+        v = captured["v"][b:b + 1].float().cpu().numpy()
+        idx = captured["idx"][b:b + 1].cpu().numpy()
+        ref = oracle.sqdk_fp32(q, k, v, idx, captured["scale"])
+        err = np.abs(captured["o"][b:b + 1].float().cpu().numpy() - ref)
+        worst_max, worst_mean = max(worst_max, float(err.max())), max(worst_mean, float(err.mean()))
+    res.update(max_abs=worst_max, mean_abs=worst_mean, bar={"max_abs": 2e-2, "mean_abs": 2e-3},
+               ok=bool(worst_max <= 2e-2 and worst_mean <= 2e-3))
+    return res
+
+
+# ---------------------------------------------------------------------------
+# long context: one sequence, sequence-sharded over the ranks
+# ---------------------------------------------------------------------------
+
+
+def _long_block(args, S, dev, fp32_gate=False):
+    import torch
+
+    from hspmn_b200 import HSPMNBlock, HSPMNConfig, seed_everything
+
+    seed_everything(42)
+    cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads, sparsity_k=args.sparsity,
+                      max_seq_len=S)
+    model = HSPMNBlock(cfg).to(dev, dtype=torch.bfloat16).eval()
+    model.router.fp32_gate = fp32_gate
+    return model
+
+
+def long_parity(args, rank, world, dev):
+    """Sequence-sharded forward over every rank at S=32768 against the plain
+    one-GPU block forward on rank 0 (same weights and input on all ranks).
+    The router's fp32 gate kernel is used on both sides: its logits depend
+    only on their own row, so both sides select the same positions whatever
+    GEMM shapes the projections get."""
+    import torch
+    import torch.distributed as dist
+
+    from hspmn_b200.parallel import SequenceShardedBlock, ZigZagPlan
+
+    S = LONG_PARITY_SEQ
+    model = _long_block(args, S, dev, fp32_gate=True)
+    g = torch.Generator(device=dev).manual_seed(3000)
+    x = torch.randn(1, S, args.dim, device=dev, dtype=torch.bfloat16, generator=g)
+    plan = ZigZagPlan(S, world)
+    with torch.no_grad():
+        y_local, aux = SequenceShardedBlock(model, plan).forward(plan.shard(x, rank))
+        parts = torch.empty((world,) + tuple(y_local.shape), dtype=y_local.dtype, device=dev)
+        dist.all_gather_into_tensor(parts, y_local.contiguous())
+        res = None
+        if rank == 0:
+            y_ref, aux_ref = model(x)
+            y = plan.unshard(list(parts.unbind(0)))
+            err = (y.float() - y_ref.float()).abs()
+            res = {"seq_len": S, "ranks": world, "max_abs": err.max().item(), "mean_abs": err.mean().item(),
+                   "aux_abs": abs(aux.item() - aux_ref.item()), "bar": {"max_abs": 3e-2, "mean_abs": 1e-3},
+                   "router_gate": "fp32 gate kernel (row-independent logits) on both sides"}
+            res["ok"] = bool(res["max_abs"] <= 3e-2 and res["mean_abs"] <= 1e-3 and res["aux_abs"] <= 1e-3)
+    del model, x, y_local, parts
+    return res
+
+
+def long_context(args, rank, world, dev, steps):
+    """Timed S=262144 sequence-sharded forward (strong scaling: the same
+    sequence whatever the rank count), then the K/V exchange timed alone."""
+    import torch
+    import torch.distributed as dist
+
+    from hspmn_b200 import ops
+    from hspmn_b200.parallel import SequenceShardedBlock, ZigZagPlan, _all_gather_rows_async
+
+    S = LONG_SEQ
+    model = _long_block(args, S, dev)
+    plan = ZigZagPlan(S, world)
+    sb = SequenceShardedBlock(model, plan)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x_local = torch.randn(1, 2 * plan.chunk, args.dim, device=dev, dtype=torch.bfloat16, generator=g)
+    with torch.no_grad():
+        for _ in range(3):
+            sb.forward(x_local)
+        barrier(world)
+        launches0 = ops.LaunchStats.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ops.KernelTimer() as kt:
+            e0.record()
+            for _ in range(steps):
+                sb.forward(x_local)
+            e1.record()
+        torch.cuda.synchronize()
+        launches = ops.LaunchStats.launches - launches0
+        ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+        kres = kt.results()
+        sq = kres.get("sqdk_fwd", {"launches": 1, "ms": float("nan")})
+        sq_ms = max_over_ranks(sq["ms"] / max(1, sq["launches"]), world, dev)
+        # the K/V exchange alone: both all-gathers of one forward, nothing to overlap
+        hd = args.dim // args.heads
+        kv = torch.randn(1, 2 * plan.chunk, args.kv_heads, hd, device=dev, dtype=torch.bfloat16, generator=g)
+        for _ in range(3):
+            _all_gather_rows_async(kv, plan, None)()
+        barrier(world)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        a0.record()
+        for _ in range(reps):
+            fk = _all_gather_rows_async(kv, plan, None)
+            fv = _all_gather_rows_async(kv, plan, None)
+            fk(), fv()
+        a1.record()
+        torch.cuda.synchronize()
+        ag_ms = max_over_ranks(a0.elapsed_time(a1), world, dev) / reps
+    recv_bytes = 2 * (world - 1) * 2 * plan.chunk * args.kv_heads * hd * 2
+    res = {"seq_len": S, "ranks": world, "ms_per_forward": ms, "tok_s": S / (ms / 1e3),
+           "scaling": "strong", "sqdk_ms_max_rank": sq_ms, "kv_exchange_ms": ag_ms,
+           "kv_exchange_GB_s_per_rank": recv_bytes / (ag_ms / 1e3) / 1e9 if world > 1 else None,
+           "kv_exchange_note": "K and V of all ranks into local HBM (all-gather + point-to-point), timed alone",
+           "steps": steps, "gpu_launches": launches,
+           "kernels_rank0": {n: {"launches": r["launches"], "ms_per_launch": r["ms"] / max(1, r["launches"])}
+                             for n, r in kres.items()}}
+    del model, sb, x_local, kv
+    return res
+
+
+# ---------------------------------------------------------------------------
+# standalone SQDK sparsity sweep and GPU comparators
+# ---------------------------------------------------------------------------
+
+
+def _sqdk_flops(idx, H, hd):
+    return 4.0 * hd * H * float((idx + 1).sum().item())
+
+
+def _time_cuda(fn, reps=5, warm=2):
+    import torch
+
+    for _ in range(warm):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gpu_comparators(q_sel, k, v, idx, scale, ours_ms, flops, eager=True):
+    """The same SQDK attention through library kernels on this GPU: torch
+    SDPA (memory-efficient and cuDNN backends) with a boolean [B,1,K,S] mask,
+    and the reference's own dense-masked PyTorch pattern
+    (test_kernels_v2_1.py:34-65) in bf16. K/V heads are repeated for grouped
+    queries. Each result gives ms, algorithmic TFLOP/s (the same numerator as
+    this library's kernel) and this library's speed-up over it."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    B, K, H, hd = q_sel.shape
+    S = k.shape[1]
+    G = H // k.shape[2]
+    qh = q_sel.permute(0, 2, 1, 3)
+    kh = k.repeat_interleave(G, dim=2).permute(0, 2, 1, 3) if G > 1 else k.permute(0, 2, 1, 3)
+    vh = v.repeat_interleave(G, dim=2).permute(0, 2, 1, 3) if G > 1 else v.permute(0, 2, 1, 3)
+    allowed = (torch.arange(S, device=idx.device)[None, None, None, :] <= idx[:, None, :, None])
+    out = {}
+
+    def record(name, fn):
+        try:
+            with torch.no_grad():
+                ms = _time_cuda(fn)
+            out[name] = {"ms": ms, "TFLOP_s": flops / (ms / 1e3) / 1e12, "ours_speedup": ms / ours_ms}
+        except Exception as e:  # a backend that does not take this mask or shape
+            out[name] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+        torch.cuda.synchronize()
+
+    for name, be in (("torch_sdpa_efficient", SDPBackend.EFFICIENT_ATTENTION),
+                     ("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION)):
+        def run(be=be):
+            with sdpa_kernel([be]):
+                return F.scaled_dot_product_attention(qh, kh, vh, attn_mask=allowed, scale=scale)
+        record(name, run)
+    if eager:
+        def eager_pattern():
+            s = torch.matmul(qh, kh.transpose(-2, -1)) * scale
+            s = s.masked_fill(~allowed, float("-inf"))
+            return torch.matmul(F.softmax(s, dim=-1), vh)
+        record("torch_eager_reference_pattern", eager_pattern)
+    out["note"] = ("library kernels on the same inputs and GPU; the reference's Triton kernel cannot be run here "
+                   "(the reference is not pip-installable and its sources do not travel to the GPU box)")
+    return out
+
+
+def sqdk_sweep(args, dev, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5), steps=None,
+               comparators=(0.05, 0.2)):
+    """Standalone router / gather / SQDK / scatter at B=8, S=32768, H=Hkv=16,
+    hd=128 for each sparsity; returns one dict per k."""
+    import torch
+
+    from hspmn_b200 import ops
+
+    hd = 128
+    steps = steps or args.steps
+    peaks, peak_src = load_peaks()
+    g = torch.Generator(device=dev).manual_seed(7)
+    q = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    logits = torch.randn(B, S, device=dev, dtype=torch.float32, generator=g)
+    rows = []
+    for frac in fracs:
+        K = max(1, int(S * frac))
+
+        def step():
+            idx, _ = ops.router_topk(logits, None, K, torch.float32)
+            qs = ops.gather_rows(q, idx)
+            o = ops.sqdk_fwd(qs, k, v, idx, hd ** -0.5)
+            return ops.scatter_rows(o, idx, S), idx, qs
+
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                _, idx, qs = step()
+            flops = _sqdk_flops(idx, H, hd)
+            torch.cuda.synchronize()
+            with ops.KernelTimer() as kt:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    step()
+                e1.record()
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        res = {n: r["ms"] / r["launches"] for n, r in kt.results().items()}
+        tf = flops / (res["sqdk_fwd"] / 1e3) / 1e12
+        gather_b = 2 * B * K * H * hd * 2 + B * K * 8
+        scatter_b = B * K * H * hd * 2 + B * S * H * hd * 2 + B * K * 8
+        router_b = B * S * 4 + B * K * 8 + B * S
+        row = {"k": frac, "K": K, "sqdk_ms": res["sqdk_fwd"], "sqdk_TFLOP_s": tf,
+               "sqdk_frac_of_burst_peak": tf / float(peaks["bf16_tflops"]),
+               "router_us": res["router_topk"] * 1e3, "router_GB_s": router_b / (res["router_topk"] / 1e3) / 1e9,
+               "gather_GB_s": gather_b / (res["gather_rows"] / 1e3) / 1e9,
+               "scatter_GB_s": scatter_b / (res["scatter_rows"] / 1e3) / 1e9,
+               "gather_frac_of_hbm": gather_b / (res["gather_rows"] / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
+               "scatter_frac_of_hbm": scatter_b / (res["scatter_rows"] / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
+               "ms_per_step": ms / steps}
+        if frac in comparators:
+            row["gpu_comparator"] = gpu_comparators(qs, k, v, idx, hd ** -0.5, res["sqdk_fwd"], flops,
+                                                    eager=frac <= 0.05)
+        rows.append(row)
+        free_cuda()
+    del q, k, v, logits
+    return {"workload": f"B={B} S={S} H={H} Hkv={Hkv} hd={hd}, router on f32 logits",
+            "peak_source": f"{peak_src} (bf16 burst, HBM copy)", "rows": rows}
+
+
+# ---------------------------------------------------------------------------
+# our arm: the block step
+# ---------------------------------------------------------------------------
+
+
 def run_block(args):
     import torch
 
     from hspmn_b200 import HSPMNBlock, HSPMNConfig, ops, seed_everything
 
     rank, world, local_rank = dist_env()
-    dev = init_dist(world, local_rank)
+    dev = init_dist(world, local_rank, always_group=not args.no_extras)
     seed_everything(42)
     cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads, sparsity_k=args.sparsity,
                       max_seq_len=args.seq_len)
@@ -377,12 +785,17 @@ def run_block(args):
             run_pipeline(args.e2e_steps, e0)
             e1.record(comp)
             torch.cuda.synchronize()
-            e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+            e2e_ms_rank = e0.elapsed_time(e1)
+            e2e_ms = max_over_ranks(e2e_ms_rank, world, dev)
+            bi = x_host.numel() * x_host.element_size()
+            bo = out_host[0].numel() * out_host[0].element_size() + 2
             e2e = {"value": B * S * args.e2e_steps * world / (e2e_ms / 1e3), "unit": "tok/s",
-                   "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-                   "d2h_bytes_per_step": out_host[0].numel() * out_host[0].element_size() + 2,
+                   "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
                    "pipeline": "2-deep: upload of step i+1 and download of step i-1 overlap forward i",
-                   "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps}
+                   "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
+                   "host_link_GB_s_per_rank": (bi + bo) * args.e2e_steps / (e2e_ms / 1e3) / 1e9,
+                   "host_link_GB_s_all_ranks": (bi + bo) * args.e2e_steps * world / (e2e_ms / 1e3) / 1e9}
+            del x_host, out_host, x_dev
 
         # the opt-in fp32 gate kernel next to the module's cuBLAS gate (nn.Linear(dim, 1)),
         # both over the whole x (larger than L2) of this GPU
@@ -390,17 +803,34 @@ def run_block(args):
         gate_times = {}
         for name, fn in (("gate_logits", lambda: ops.gate_logits(x, gate_w, gate_b)),
                          ("cublas_gate", lambda: model.router.gate(x))):
-            for _ in range(3):
-                fn()
-            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            g0.record()
-            for _ in range(10):
-                fn()
-            g1.record()
-            torch.cuda.synchronize()
-            gate_times[name] = g0.elapsed_time(g1) / 10
+            gate_times[name] = _time_cuda(fn, reps=10, warm=3)
+
+        extras = {}
+        if not args.no_extras:
+            if rank == 0:
+                extras["headline_parity"] = headline_parity(model, x)
+            del model, x
+            free_cuda()
+            barrier(world)
+            extras["long_parity"] = long_parity(args, rank, world, dev)
+            free_cuda()
+            barrier(world)
+            extras["long_context"] = long_context(args, rank, world, dev, args.long_steps)
+            free_cuda()
+            barrier(world)
+            if world == 1:
+                sweep = sqdk_sweep(args, dev)
+                extras["sqdk_sweep"] = sweep
+                free_cuda()
+                # comparators at the headline attention shape (B=64, K=820, S=4096, GQA 4)
+                extras["gpu_comparator_headline"] = headline_comparators(args, dev)
+                free_cuda()
 
     if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    elif not args.no_extras:
         import torch.distributed as dist
         dist.destroy_process_group()
     if rank != 0:
@@ -410,7 +840,8 @@ def run_block(args):
     sq = kres.get("sqdk_fwd", {"launches": 0, "ms": float("nan")})
     sq_ms = sq["ms"] / max(1, sq["launches"])
     achieved = sqdk_flops / (sq_ms / 1e3) / 1e12
-    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     wl_tag = f"B{B}_S{S}_D{D}_H{args.heads}_Hkv{args.kv_heads}"
     traffic = profiled_traffic("sqdk_fwd", wl_tag)
     esz = 2
@@ -418,26 +849,25 @@ def run_block(args):
     for name, r in kres.items():
         per = r["ms"] / max(1, r["launches"])
         kernels[name] = {"launches": r["launches"], "ms_per_launch": per}
-    if "gather_rows" in kernels:
-        gb = 2 * B * k_sel * D * esz + B * k_sel * 8
-        kernels["gather_rows"]["GB_s"] = gb / (kernels["gather_rows"]["ms_per_launch"] / 1e3) / 1e9
+    hbm = float(peaks["hbm_gbs"])
+
+    def gbs(name, nbytes):
+        if name in kernels:
+            v = nbytes / (kernels[name]["ms_per_launch"] / 1e3) / 1e9
+            kernels[name]["GB_s"] = v
+            kernels[name]["frac_of_hbm"] = v / hbm
+
+    gbs("gather_rows", 2 * B * k_sel * D * esz + B * k_sel * 8)
     if "rope_gather_rows" in kernels:
-        # two launches per forward: the K routed query rows (D elements each) and all S key
-        # rows (Hkv * hd elements each); each reads its rows and indices and writes its rows
+        # the K routed query rows (D elements each, indices read)
+        gbs("rope_gather_rows", 2 * B * k_sel * D * esz + B * k_sel * 8)
+    if "rope_rows" in kernels:
+        # RoPE over all S key rows (Hkv * hd elements each) in one pass, positions implied
         kv_row = (D // args.heads) * args.kv_heads
-        gb_step = (2 * B * k_sel * D * esz + B * k_sel * 8) + (2 * B * S * kv_row * esz + B * S * 8)
-        steps_seen = max(1, kernels.get("sqdk_fwd", {}).get("launches", 1))
-        per_step = max(1, kernels["rope_gather_rows"]["launches"] // steps_seen)
-        kernels["rope_gather_rows"]["GB_s"] = (gb_step / per_step) / (kernels["rope_gather_rows"]["ms_per_launch"] / 1e3) / 1e9
-    if "scatter_add_rows" in kernels:
-        gb = 3 * B * k_sel * D * esz + B * k_sel * 8
-        kernels["scatter_add_rows"]["GB_s"] = gb / (kernels["scatter_add_rows"]["ms_per_launch"] / 1e3) / 1e9
-    if "scatter_rows" in kernels:
-        gb = B * k_sel * D * esz + B * S * D * esz + B * k_sel * 8
-        kernels["scatter_rows"]["GB_s"] = gb / (kernels["scatter_rows"]["ms_per_launch"] / 1e3) / 1e9
-    if "router_topk" in kernels:
-        gb = B * S * esz + B * k_sel * 8 + B * S
-        kernels["router_topk"]["GB_s"] = gb / (kernels["router_topk"]["ms_per_launch"] / 1e3) / 1e9
+        gbs("rope_rows", 2 * B * S * kv_row * esz)
+    gbs("scatter_add_rows", 3 * B * k_sel * D * esz + B * k_sel * 8)
+    gbs("scatter_rows", B * k_sel * D * esz + B * S * D * esz + B * k_sel * 8)
+    gbs("router_topk", B * S * esz + B * k_sel * 8 + B * S)
     if "sqdk_fwd" in kernels:
         kernels["sqdk_fwd"]["TFLOP_s"] = achieved
         kernels["sqdk_fwd"]["algorithmic_flops"] = sqdk_flops
@@ -446,9 +876,9 @@ def run_block(args):
     for name, out_bytes in (("gate_logits", 4), ("cublas_gate", esz)):
         gb = B * S * D * esz + D * esz + B * S * out_bytes
         ms = gate_times[name]
-        gate[name] = {"ms_per_launch": ms, "GB_s": gb / (ms / 1e3) / 1e9,
-                      "frac_of_hbm": gb / (ms / 1e3) / 1e9 / float(peaks["hbm_gbs"])}
+        gate[name] = {"ms_per_launch": ms, "GB_s": gb / (ms / 1e3) / 1e9, "frac_of_hbm": gb / (ms / 1e3) / 1e9 / hbm}
 
+    sm_mhz = clock_info.get("sm_mhz") if clock_info else None
     value = B * S * args.steps * world / (ms_total / 1e3)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -458,7 +888,12 @@ def run_block(args):
         "config": workload_config(args),
         "roofline": {"bound": "tensor", "kernel": "sqdk_fwd", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_src} bf16 dense, sustained (kernel timed inside a long step)",
+                     "peak_source": f"{peak_src} bf16 dense, burst (cuBLAS 8192^3 best of 10)",
+                     "frac_of_sustained_peak": achieved / peak_sus,
+                     "sustained_peak": peak_sus,
+                     "sustained_peak_clock_mhz": (peaks.get("clocks_under_load") or {}).get("sm_mhz_median"),
+                     "kernel_clock_mhz": sm_mhz,
+                     "ms_x_mhz_per_launch": sq_ms * sm_mhz if sm_mhz else None,
                      "flops_per_launch": sqdk_flops, "ms_per_launch": sq_ms, "k_selected": k_sel},
         "kernels": kernels,
         "router_gate": dict(gate, note="opt-in fp32 gate (router.fp32_gate) vs the default cuBLAS bf16 gate; "
@@ -468,75 +903,58 @@ def run_block(args):
     }
     if e2e is not None:
         line["e2e"] = e2e
+    line.update(extras)
     if world == 1 and not args.no_cpu_baseline:
-        tok_s, sample, cores, _ = cpu_block_sample(args, args.cpu_sample_seconds)
-        line["cpu_baseline"] = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+        line["cpu_baseline"] = cpu_reference_sample(args, seconds=args.cpu_sample_seconds)
+        line["cpu_baseline_oracle"] = cpu_oracle_sample(args, args.cpu_sample_seconds)
+        line["cpu_sqdk_cfg1"] = cpu_sqdk_cfg1()
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------------------
-# standalone SQDK sparsity sweep
-# ---------------------------------------------------------------------------
-
-
-def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
+def headline_comparators(args, dev):
+    """Library comparators at the headline attention shape: this library's
+    SQDK vs torch SDPA / the eager reference pattern on the same q_sel, K, V
+    and indices (random sorted selection of K = int(S * k) rows)."""
     import torch
 
     from hspmn_b200 import ops
 
-    rank, world, local_rank = dist_env()
-    dev = init_dist(world, local_rank)
-    hd = 128
-    peaks, peak_src = load_peaks()
-    g = torch.Generator(device=dev).manual_seed(7 + rank)
-    q = torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
+    B, S, H, Hkv = args.batch, args.seq_len, args.heads, args.kv_heads
+    hd = args.dim // H
+    K = max(1, int(S * args.sparsity))
+    g = torch.Generator(device=dev).manual_seed(13)
+    q = torch.randn(B, K, H, hd, device=dev, dtype=torch.bfloat16, generator=g)
     k = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
     v = torch.randn(B, S, Hkv, hd, device=dev, dtype=torch.bfloat16, generator=g)
-    logits = torch.randn(B, S, device=dev, dtype=torch.float32, generator=g)
-    for frac in fracs:
-        K = max(1, int(S * frac))
+    idx = torch.sort(torch.rand(B, S, device=dev, generator=g).argsort(dim=1)[:, :K], dim=1)[0]
+    scale = hd ** -0.5
+    with torch.no_grad():
+        ours = _time_cuda(lambda: ops.sqdk_fwd(q, k, v, idx, scale), reps=10, warm=3)
+    flops = _sqdk_flops(idx, H, hd)
+    res = gpu_comparators(q, k, v, idx, scale, ours, flops)
+    res["ours"] = {"ms": ours, "TFLOP_s": flops / (ours / 1e3) / 1e12}
+    res["workload"] = f"SQDK B={B} K={K} S={S} H={H} Hkv={Hkv} hd={hd} (random sorted selection)"
+    return res
 
-        def step():
-            idx, _ = ops.router_topk(logits, None, K, torch.float32)
-            qs = ops.gather_rows(q, idx)
-            o = ops.sqdk_fwd(qs, k, v, idx, hd ** -0.5)
-            return ops.scatter_rows(o, idx, S), idx
 
-        with torch.no_grad():
-            for _ in range(args.warmup):
-                _, idx = step()
-            flops = 4.0 * hd * H * float((idx + 1).sum().item())
-            barrier(world)
-            with ops.KernelTimer() as kt:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                for _ in range(args.steps):
-                    step()
-                e1.record()
-            torch.cuda.synchronize()
-        ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-        res = {n: r["ms"] / r["launches"] for n, r in kt.results().items()}
-        if rank == 0:
-            tf = flops / (res["sqdk_fwd"] / 1e3) / 1e12
-            gather_b = 2 * B * K * H * hd * 2 + B * K * 8  # noqa: E501 (rows are H*hd wide)
-            scatter_b = B * K * H * hd * 2 + B * S * H * hd * 2 + B * K * 8
-            print(json.dumps({
-                "metric": "standalone SQDK: attention TFLOP/s and gather/scatter GB/s", "workload":
-                f"B={B} S={S} H={H} Hkv={Hkv} hd={hd} k={frac} (K={K}), router on f32 logits", "n_gpus": world,
-                "value": tf, "unit": "TFLOP/s", "frac_of_peak": tf / float(peaks["bf16_tflops"]),
-                "peak_source": f"{peak_src} bf16 dense, burst", "ms_per_step": ms / args.steps,
-                "router_us": res["router_topk"] * 1e3,
-                "gather_GB_s": gather_b / (res["gather_rows"] / 1e3) / 1e9,
-                "scatter_GB_s": scatter_b / (res["scatter_rows"] / 1e3) / 1e9,
-                "hbm_peak_GB_s": float(peaks["hbm_gbs"]), "sqdk_ms": res["sqdk_fwd"]}), flush=True)
+# ---------------------------------------------------------------------------
+# standalone workloads
+# ---------------------------------------------------------------------------
+
+
+def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
+    rank, world, local_rank = dist_env()
+    dev = init_dist(world, local_rank)
+    res = sqdk_sweep(args, dev, B, S, H, Hkv, fracs, comparators=fracs if len(fracs) == 1 else (0.05, 0.2))
+    if rank == 0:
+        for row in res["rows"]:
+            print(json.dumps({"metric": "standalone SQDK: attention TFLOP/s and gather/scatter GB/s",
+                              "workload": res["workload"] + f", k={row['k']} (K={row['K']})", "n_gpus": 1,
+                              "value": row["sqdk_TFLOP_s"], "unit": "TFLOP/s", "peak_source": res["peak_source"],
+                              **row}), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
-
-
-# ---------------------------------------------------------------------------
-# SQDK backward (training path of the contextual stream)
-# ---------------------------------------------------------------------------
 
 
 def run_sqdk_bwd(args):
@@ -594,72 +1012,27 @@ def run_sqdk_bwd(args):
         dist.destroy_process_group()
 
 
-# ---------------------------------------------------------------------------
-# long context: one sequence, sequence-sharded over the ranks
-# ---------------------------------------------------------------------------
-
-
 def run_long(args):
-    import torch
-
-    from hspmn_b200 import HSPMNBlock, HSPMNConfig, ops, seed_everything
-    from hspmn_b200.parallel import SequenceShardedBlock, ZigZagPlan
+    import torch.distributed as dist
 
     rank, world, local_rank = dist_env()
-    if world == 1:
-        # a one-rank process group keeps the code path identical to N > 1
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29531")
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-        dev = torch.device("cuda", local_rank)
-    else:
-        dev = init_dist(world, local_rank)
-    S = args.seq_len
-    seed_everything(42)
-    cfg = HSPMNConfig(dim=args.dim, num_heads=args.heads, num_kv_heads=args.kv_heads, sparsity_k=args.sparsity,
-                      max_seq_len=S)
-    model = HSPMNBlock(cfg).to(dev, dtype=torch.bfloat16).eval()
-    plan = ZigZagPlan(S, world)
-    sb = SequenceShardedBlock(model, plan)
-    g = torch.Generator(device=dev).manual_seed(2000 + rank)
-    x_local = torch.randn(1, 2 * plan.chunk, args.dim, device=dev, dtype=torch.bfloat16, generator=g)
-    with torch.no_grad():
-        for _ in range(args.warmup):
-            sb.forward(x_local)
-        barrier(world)
-        launches0 = ops.LaunchStats.launches
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ops.KernelTimer() as kt:
-            e0.record()
-            for _ in range(args.steps):
-                sb.forward(x_local)
-            e1.record()
-        torch.cuda.synchronize()
-        launches = ops.LaunchStats.launches - launches0
-        ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-        kres = kt.results()
-        sq = kres.get("sqdk_fwd", {"launches": 1, "ms": float("nan")})
-        sq_ms = max_over_ranks(sq["ms"] / max(1, sq["launches"]), world, dev)
-    import torch.distributed as dist
+    dev = init_dist(world, local_rank, always_group=True)
+    par = long_parity(args, rank, world, dev)
+    free_cuda()
+    barrier(world)
+    res = long_context(args, rank, world, dev, args.long_steps)
+    barrier(world)
     dist.destroy_process_group()
     if rank == 0:
-        peaks, peak_src = load_peaks()
-        value = S * args.steps / (ms / 1e3)
         print(json.dumps({
-            "metric": "long-context HSPMNBlock tok/s (one sequence, sequence-sharded)", "value": value,
-            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
-            "config": {"workload": f"HSPMNBlock eval forward, B=1 S={S} dim={args.dim} heads={args.heads} "
+            "metric": "long-context HSPMNBlock tok/s (one sequence, sequence-sharded)", "value": res["tok_s"],
+            "unit": "tok/s", "n_gpus": world, "steps": res["steps"], "ms_per_step": res["ms_per_forward"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: x ~ N(0,1), default-init weights (seed 42)",
+            "config": {"workload": f"HSPMNBlock eval forward, B=1 S={LONG_SEQ} dim={args.dim} heads={args.heads} "
                                    f"kv_heads={args.kv_heads} k={args.sparsity}, zig-zag sequence shards",
-                       "seq_len": S, "parallelism": f"sequence-sharded x{world}, all-gather of logits and K/V"},
-            "sqdk_ms_per_launch_max_rank": sq_ms, "gpu_launches": launches,
-            "kernels_rank0": {n: {"launches": r["launches"], "ms_per_launch": r["ms"] / max(1, r["launches"])}
-                              for n, r in kres.items()},
-            "peak_source": peak_src}), flush=True)
+                       "seq_len": LONG_SEQ, "parallelism": f"sequence-sharded x{world}"},
+            "long_context": res, "long_parity": par}), flush=True)
 
 
 def main():

@@ -4,7 +4,7 @@ The library is compiled in-tree (next to the Python package) with nvcc for
 ``sm_100a`` only; the product has no other target. Rebuilds only when a
 source under ``csrc/`` or ``include/`` is newer than the library.
 
-    python hspmn-v2.1_b200/build_native.py [--force] [--debug]
+    python hspmn-v2.1_b200/build_native.py [--force] [-v]
 """
 
 from __future__ import annotations
@@ -50,16 +50,14 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force: bool = False, debug: bool = False, verbose: bool = False) -> str:
-    if not force and not debug and up_to_date():
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and up_to_date():
         return LIB
-    out = LIB if not debug else LIB.replace(".so", "_debug.so")
+    out = LIB
     cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC,
            os.path.join(CSRC, "hspmn_sm100.cu"), "-o", out + ".tmp"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
-    if debug:
-        cmd.insert(1, "-DHSPMN_DEBUG=1")
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
@@ -72,7 +70,6 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> st
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
-    ap.add_argument("--debug", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
-    print(build(force=a.force, debug=a.debug, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose))

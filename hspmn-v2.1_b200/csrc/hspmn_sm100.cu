@@ -394,6 +394,42 @@ int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t src_ss, int 
   return launch_status();
 }
 
+int hspmn_rope_rows(const void* src, int64_t src_sb, int64_t src_ss, const void* cos_tab, const void* sin_tab,
+                    int64_t tab_ss, int64_t tab_rows, int64_t pos0, void* dst, int64_t dst_sb, int64_t dst_ss,
+                    int64_t B, int64_t S, int64_t H, int64_t hd, int dtype, void* stream) {
+  if (!src || !cos_tab || !sin_tab || !dst || B < 0 || S < 0 || H < 1 || hd < 2 || pos0 < 0)
+    return HSPMN_ERR_INVALID;
+  if (!valid_dtype(dtype)) return HSPMN_ERR_DTYPE;
+  if (src_sb < 0 || src_ss < 0 || dst_sb < 0 || dst_ss < 0 || tab_ss < hd || pos0 + S > tab_rows)
+    return HSPMN_ERR_INVALID;
+  if (B == 0 || S == 0) return HSPMN_OK;
+  if (H * hd > 0x7FFFFFFF) return HSPMN_ERR_INVALID;
+  const int64_t es = dtype == HSPMN_F32 ? 4 : 2;
+  const int64_t vec = 16 / es;
+  if (hd % (2 * vec) != 0) return HSPMN_ERR_UNSUPPORTED;
+  if (!aligned(src, 16) || !aligned(dst, 16) || !aligned(cos_tab, 16) || !aligned(sin_tab, 16) ||
+      (src_sb * es) % 16 || (src_ss * es) % 16 || (dst_sb * es) % 16 || (dst_ss * es) % 16 || (tab_ss * es) % 16)
+    return HSPMN_ERR_ALIGN;
+  if (int rc = check_device()) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t warps = (B * S + 1) / 2;
+  int64_t blocks = (warps + kRowWarps - 1) / kRowWarps;
+  blocks = std::min<int64_t>(blocks, static_cast<int64_t>(sms) * 8);
+  const unsigned g = static_cast<unsigned>(blocks);
+#define HSPMN_ROPE_ROWS_LAUNCH(T)                                                                                    \
+  rope_rows_kernel<T><<<g, kRowThreads, 0, st>>>(static_cast<const T*>(src), src_sb, src_ss,                        \
+                                                 static_cast<const T*>(cos_tab), static_cast<const T*>(sin_tab),     \
+                                                 tab_ss, pos0, static_cast<T*>(dst), dst_sb, dst_ss, B, S,           \
+                                                 static_cast<int>(H), static_cast<int>(hd))
+  if (dtype == HSPMN_BF16) HSPMN_ROPE_ROWS_LAUNCH(__nv_bfloat16);
+  else if (dtype == HSPMN_F16) HSPMN_ROPE_ROWS_LAUNCH(__half);
+  else HSPMN_ROPE_ROWS_LAUNCH(float);
+#undef HSPMN_ROPE_ROWS_LAUNCH
+  return launch_status();
+}
+
 int hspmn_scatter_add_rows(const void* src, int64_t src_sb, int64_t src_sk, const int64_t* idx, int64_t idx_sb,
                            void* dst, int64_t dst_sb, int64_t dst_ss, int64_t B, int64_t S, int64_t K,
                            int64_t row_elems, int dtype, void* stream) {
@@ -428,7 +464,7 @@ int sqdk_fwd_impl(const void* q, const int64_t* qs, const void* k, const int64_t
                   const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o, const int64_t* os,
                   float* lse, int64_t lse_sb, int64_t lse_sk, int64_t B, int64_t K, int64_t S, int64_t H,
                   int64_t Hkv, int64_t hd, int dtype, float sm_scale, void* workspace, size_t workspace_bytes,
-                  void* stream) {
+                  bool static_scratch, void* stream) {
   if (!q || !k || !v || !idx || !o || !qs || !ks || !vs || !os) return HSPMN_ERR_INVALID;
   if (lse && (lse_sk < H || lse_sb < 0)) return HSPMN_ERR_INVALID;
   if (B < 0 || K < 0 || S < 1 || H < 1 || Hkv < 1 || !(sm_scale > 0.0f) || !std::isfinite(sm_scale))
@@ -449,6 +485,15 @@ int sqdk_fwd_impl(const void* q, const int64_t* qs, const void* k, const int64_t
 
   SqdkPlan pl;
   if (int rc = sqdk_plan(B, K, S, H, Hkv, hd, &pl)) return rc;
+  if (static_scratch) {
+    // hspmn_sqdk_fwd_noalloc: the split-KV partials go to the library's own
+    // device array, looked up only for launches that split
+    if (pl.ws_bytes > static_cast<int64_t>(HSPMN_SQDK_NOALLOC_SCRATCH_BYTES)) return HSPMN_ERR_SCRATCH;
+    if (pl.ws_bytes > 0) {
+      if (int rc = sqdk_scratch(&workspace)) return rc;
+      workspace_bytes = HSPMN_SQDK_NOALLOC_SCRATCH_BYTES;
+    }
+  }
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < static_cast<size_t>(pl.ws_bytes)))
     return HSPMN_ERR_INVALID;
   if (pl.ws_bytes > 0 && !aligned(workspace, 16)) return HSPMN_ERR_ALIGN;
@@ -523,7 +568,7 @@ int hspmn_sqdk_fwd(const void* q, const int64_t* qs, const void* k, const int64_
                    const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
                    int dtype, float sm_scale, void* workspace, size_t workspace_bytes, void* stream) {
   return sqdk_fwd_impl(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, nullptr, 0, 0, B, K, S, H, Hkv, hd, dtype,
-                       sm_scale, workspace, workspace_bytes, stream);
+                       sm_scale, workspace, workspace_bytes, false, stream);
 }
 
 int hspmn_sqdk_fwd_lse(const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
@@ -533,7 +578,7 @@ int hspmn_sqdk_fwd_lse(const void* q, const int64_t* qs, const void* k, const in
                        size_t workspace_bytes, void* stream) {
   if (!lse) return HSPMN_ERR_INVALID;
   return sqdk_fwd_impl(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, lse, lse_sb, lse_sk, B, K, S, H, Hkv, hd,
-                       dtype, sm_scale, workspace, workspace_bytes, stream);
+                       dtype, sm_scale, workspace, workspace_bytes, false, stream);
 }
 
 int64_t hspmn_sqdk_bwd_workspace_size(int64_t B, int64_t K, int64_t H, int64_t hd) {
@@ -712,17 +757,10 @@ int hspmn_sqdk_fwd_noalloc(const void* q, const int64_t* qs, const void* k, cons
                            const int64_t* vs, const int64_t* idx, int64_t idx_sb, int64_t idx_sk, void* o,
                            const int64_t* os, int64_t B, int64_t K, int64_t S, int64_t H, int64_t Hkv, int64_t hd,
                            int dtype, float sm_scale, void* stream) {
-  if (int rc = check_device()) return rc;
-  void* scratch = nullptr;
-  if (int rc = sqdk_scratch(&scratch)) return rc;
-  // hspmn_sqdk_workspace_size gives 0 for shapes hspmn_sqdk_fwd rejects, so
-  // its own validation reports those.
-  const bool shape_ok = B > 0 && K > 0 && S > 0 && hd >= 8 && hd <= 128 && hd % 8 == 0;
-  const int64_t need = shape_ok ? hspmn_sqdk_workspace_size(B, K, S, H, Hkv, hd) : 0;
-  if (need < 0) return HSPMN_ERR_CUDA;
-  if (need > static_cast<int64_t>(HSPMN_SQDK_NOALLOC_SCRATCH_BYTES)) return HSPMN_ERR_SCRATCH;
-  return hspmn_sqdk_fwd(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, B, K, S, H, Hkv, hd, dtype, sm_scale,
-                        need > 0 ? scratch : nullptr, need > 0 ? HSPMN_SQDK_NOALLOC_SCRATCH_BYTES : 0, stream);
+  // the same validation, in the same order, as hspmn_sqdk_fwd; the static
+  // scratch stands in for the caller's workspace
+  return sqdk_fwd_impl(q, qs, k, ks, v, vs, idx, idx_sb, idx_sk, o, os, nullptr, 0, 0, B, K, S, H, Hkv, hd, dtype,
+                       sm_scale, nullptr, 0, true, stream);
 }
 
 int hspmn_device_errors(unsigned* bits, int clear, void* stream) {

@@ -235,6 +235,60 @@ __global__ void __launch_bounds__(kRowThreads) rope_gather_rows_kernel(
   }
 }
 
+// Rotary embedding of every row of a [B,S,H,hd] tensor whose position is its
+// row number (plus pos0): the K RoPE of hspmn_v2_1.py:226-227 in one pass,
+// with no index array. Each unit is one 16-byte group of a head's low half and
+// its partner group in the high half, so a thread loads x_lo, x_hi and the
+// four table groups once and writes both outputs (rope(x)[d] pairs x[d] with
+// x[d +- hd/2]). A warp covers one row per iteration, two rows in flight.
+// Every unit reads its inputs before writing, so dst may be src itself.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) rope_rows_kernel(
+    const T* src, int64_t src_sb, int64_t src_ss, const T* __restrict__ cos_t,
+    const T* __restrict__ sin_t, int64_t tab_ss, int64_t pos0, T* dst, int64_t dst_sb, int64_t dst_ss,
+    int64_t B, int64_t S, int H, int hd) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int half = hd / 2;
+  const int gph = half / V;  // 16-byte groups per half head
+  const int units = H * gph;
+  const int64_t rows = B * S;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRowWarps;
+  for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5)) * 2; r0 < rows;
+       r0 += 2 * nwarps) {
+    for (int u = lane; u < units; u += 32) {
+      const int h = u / gph;
+      const int d = (u - h * gph) * V;  // column in the low half
+      const int e = h * hd + d;
+      uint4 xl[2], xh[2], cl[2], ch[2], sl[2], sh[2];
+      int64_t bb[2], ss[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t r = min(r0 + k, rows - 1);  // a lone last row is simply done twice
+        bb[k] = r / S;
+        ss[k] = r - bb[k] * S;
+        const T* x = src + bb[k] * src_sb + ss[k] * src_ss + e;
+        const int64_t p = (pos0 + ss[k]) * tab_ss + d;
+        xl[k] = *reinterpret_cast<const uint4*>(x);
+        xh[k] = *reinterpret_cast<const uint4*>(x + half);
+        cl[k] = __ldg(reinterpret_cast<const uint4*>(cos_t + p));
+        ch[k] = __ldg(reinterpret_cast<const uint4*>(cos_t + p + half));
+        sl[k] = __ldg(reinterpret_cast<const uint4*>(sin_t + p));
+        sh[k] = __ldg(reinterpret_cast<const uint4*>(sin_t + p + half));
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (r0 + k >= rows) break;
+        T* o = dst + bb[k] * dst_sb + ss[k] * dst_ss + e;
+        const uint4 lo = rope_vec<T>(xl[k], xh[k], true, cl[k], sl[k]);
+        const uint4 hi = rope_vec<T>(xh[k], xl[k], false, ch[k], sh[k]);
+        __stcs(reinterpret_cast<uint4*>(o), lo);
+        __stcs(reinterpret_cast<uint4*>(o + half), hi);
+      }
+    }
+  }
+}
+
 // dst[b, idx[b,i], :] = T(dst[b, idx[b,i], :] + src[b,i,:]) — the residual
 // add of hspmn_v2_1.py:238 restricted to the rows the attention wrote (every
 // other row of o_proj(scatter(...)) is zero). One warp per selected row.

@@ -205,8 +205,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         dl[u] = 0.0f;
         if (qloc < p.QTb && qi < p.K) {
           const int hh = g * p.G + (c - qloc * p.G);
-          const int64_t ps = __ldg(p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk);
+          const int64_t* ib = p.idx + static_cast<int64_t>(b) * p.idx_sb;
+          const int64_t ps = __ldg(ib + static_cast<int64_t>(qi) * p.idx_sk);
           pos[u] = (ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
+          // the key block's first query came from a binary search over the
+          // row, which needs ascending positions; the key block at 0 visits
+          // every query block, so every row is checked by some CTA
+          if (hh == g * p.G && qi > 0 && ps < __ldg(ib + static_cast<int64_t>(qi - 1) * p.idx_sk))
+            raise_device_error(HSPMN_DEVERR_UNSORTED);
           const int64_t ro = static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + hh;
           lse2[u] = __ldg(p.lse + ro) * 1.4426950408889634f;
           dl[u] = __ldg(p.delta + ro);

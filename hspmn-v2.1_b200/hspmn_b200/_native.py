@@ -43,6 +43,8 @@ _SIGNATURES = {
                               ctypes.c_float, _vp, ctypes.c_size_t, _vp]),
     "hspmn_rope_gather_rows": (_int, [_vp, _i64, _i64, _int, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64,
                                       _i64, _i64, _i64, _i64, _i64, _int, _vp]),
+    "hspmn_rope_rows": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
+                               _i64, _int, _vp]),
     "hspmn_scatter_add_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _int, _vp]),
     "hspmn_device_errors": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _vp]),

@@ -255,8 +255,7 @@ class HSPMNBlock(nn.Module):
         q_sel = ops.rope_gather_rows(q_sel, idx, cos, sin, False)
         # K RoPE on every position in one pass (same rounding as the reference's
         # three tensor ops, hspmn_v2_1.py:66-68)
-        positions = torch.arange(S, device=x_norm.device).expand(B, S)
-        k = ops.rope_gather_rows(self.k_proj(x_norm).view(B, S, Hkv, hd), positions, cos, sin, False)
+        k = ops.rope_rows(self.k_proj(x_norm).view(B, S, Hkv, hd), cos, sin, 0)
         v = self.v_proj(x_norm).view(B, S, Hkv, hd)
         attn = ops.sqdk_fwd(q_sel, k, v, idx, 1.0 / math.sqrt(hd))
         return self.o_proj(attn.reshape(B, K, D))

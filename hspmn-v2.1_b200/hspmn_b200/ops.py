@@ -106,7 +106,9 @@ class KernelTimer:
 
 
 class _launch:
-    """Wraps one native call: counts it and times it when a timer is active."""
+    """Wraps one native call: an NVTX range named ``hspmn::<op>`` around it
+    (so a timeline attributes the kernels), a launch count, and CUDA-event
+    timing when a ``KernelTimer`` is active."""
 
     __slots__ = ("name", "dev", "start")
 
@@ -114,16 +116,20 @@ class _launch:
         self.name, self.dev, self.start = name, dev, None
 
     def __enter__(self):
+        torch.cuda.nvtx.range_push("hspmn::" + self.name)
         t = LaunchStats.timer
         if t is not None:
             self.start = t._begin(self.name, self.dev)
 
     def __exit__(self, exc_type, *exc):
-        if exc_type is None:
-            LaunchStats.launches += 1
-            t = LaunchStats.timer
-            if t is not None and self.start is not None:
-                t._end(self.name, self.dev, self.start)
+        try:
+            if exc_type is None:
+                LaunchStats.launches += 1
+                t = LaunchStats.timer
+                if t is not None and self.start is not None:
+                    t._end(self.name, self.dev, self.start)
+        finally:
+            torch.cuda.nvtx.range_pop()
         return False
 
 
@@ -335,6 +341,42 @@ def _(src, indices, cos, sin, src_by_position):
     return src.new_empty((src.shape[0], indices.shape[1]) + tuple(src.shape[2:]))
 
 
+@torch.library.custom_op("hspmn::rope_rows", mutates_args=())
+def rope_rows(src: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, pos0: int) -> torch.Tensor:
+    """Rotary embedding of every row of ``src`` [B,S,H,hd], row ``s`` at
+    position ``pos0 + s``: bit-identical to the K side of
+    ``apply_rotary_pos_emb`` (hspmn_v2_1.py:66-68,226-227) on the [B,S,H,hd]
+    view, without an index array. ``cos``/``sin`` are the [L,hd] (or
+    [1,1,L,hd]) tables in ``src``'s dtype with ``pos0 + S <= L``. Returns a
+    new contiguous [B,S,H,hd] tensor."""
+    dev = _require_cuda(src, cos, sin)
+    if src.dim() != 4:
+        raise ValueError("rope_rows: src must be [B,S,H,hd]")
+    B, S, H, hd = src.shape
+    cos2, sin2 = cos.reshape(-1, hd), sin.reshape(-1, hd)
+    if cos2.dtype != src.dtype or sin2.dtype != src.dtype:
+        raise TypeError("rope_rows: cos/sin must have src's dtype")
+    if cos2.stride(1) != 1 or sin2.stride(1) != 1 or cos2.stride(0) != sin2.stride(0):
+        cos2, sin2 = cos2.contiguous(), sin2.contiguous()
+    if pos0 < 0 or pos0 + S > cos2.shape[0]:
+        raise ValueError(f"rope_rows: positions [{pos0}, {pos0 + S}) outside the {cos2.shape[0]}-row table")
+    src, _ = _rows_view(src, 2)
+    out = torch.empty((B, S, H, hd), dtype=src.dtype, device=dev)
+    with _on_device(dev), _launch("rope_rows", dev):
+        rc = N.lib().hspmn_rope_rows(
+            ctypes.c_void_p(src.data_ptr()), src.stride(0), src.stride(1),
+            ctypes.c_void_p(cos2.data_ptr()), ctypes.c_void_p(sin2.data_ptr()), cos2.stride(0), cos2.shape[0],
+            int(pos0), ctypes.c_void_p(out.data_ptr()), out.stride(0), out.stride(1), B, S, H, hd,
+            dtype_code(src.dtype), _stream(dev))
+        N.check(rc, "hspmn_rope_rows")
+    return out
+
+
+@rope_rows.register_fake
+def _(src, cos, sin, pos0):
+    return src.new_empty(src.shape)
+
+
 @torch.library.custom_op("hspmn::scatter_add_rows_", mutates_args=("dst",))
 def scatter_add_rows_(dst: torch.Tensor, indices: torch.Tensor, src: torch.Tensor) -> None:
     """In place ``dst[b, indices[b,i]] += src[b,i]`` in ``dst``'s dtype (the
@@ -491,7 +533,11 @@ def sqdk_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.T
     """Gradients (dq, dk, dv) of the SQDK attention for the output gradient
     ``d_o``, given the forward's output ``o`` and ``lse`` (``sqdk_fwd_lse``).
     The backward of the reference's training path (FlexAttention with the
-    mask (q_idx >= kv_idx) & mask[b, q_idx], hspmn_v2_1.py:200-216)."""
+    mask (q_idx >= kv_idx) & mask[b, q_idx], hspmn_v2_1.py:200-216).
+    Each ``indices`` row must be ascending, as the router writes it (a key
+    block finds its first query by binary search); a row out of order sets
+    ``DEVERR_UNSORTED`` in ``device_errors()`` and its gradients are
+    incomplete."""
     dev = _require_cuda(q, k, v, indices, o, d_o, lse)
     _check_sqdk_shapes("sqdk_bwd", q, k, v, indices)
     B, K, H, hd = q.shape
@@ -552,7 +598,8 @@ class _SqdkAttention(torch.autograd.Function):
 def sqdk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
                    sm_scale: float) -> torch.Tensor:
     """Differentiable SQDK attention: ``sqdk_fwd_lse`` forward, ``sqdk_bwd``
-    backward (bf16 / f16 operands)."""
+    backward (bf16 / f16 operands). ``indices`` rows must be ascending for
+    the backward (see ``sqdk_bwd``)."""
     return _SqdkAttention.apply(q, k, v, indices, sm_scale)
 
 

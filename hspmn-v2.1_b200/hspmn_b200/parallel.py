@@ -15,8 +15,10 @@ Two layouts, one process per GPU (``torch.distributed``, NCCL on GPUs):
        logits (2 bytes per position) lets every rank run the same
        deterministic top-K kernel, so the selected positions are identical
        everywhere;
-    2. every rank computes K/V (with RoPE) for its rows; one all-gather brings
-       the whole K/V prefix into local HBM (no peer-memory loads);
+    2. every rank computes K/V (with RoPE) for its rows; an all-gather of
+       the first chunks plus point-to-point copies of the second chunks place
+       the whole K/V prefix in position order in local HBM (no peer-memory
+       loads by the kernels, no reorder copy);
     3. each rank attends the selected queries that fall in its own chunks
        (q_proj on those rows only, RoPE fused into their gather), applies
        o_proj to the attention rows and adds them into its rows of the
@@ -93,23 +95,61 @@ class ZigZagPlan:
 
 def _all_gather_rows(local: torch.Tensor, plan: ZigZagPlan, group) -> torch.Tensor:
     """All-gather a [B, 2*chunk, ...] local tensor into the full [B, S, ...]
-    sequence in position order (one collective, then one reorder copy)."""
+    sequence in position order."""
     return _all_gather_rows_async(local, plan, group)()
 
 
+def _group_peer(group, group_rank: int) -> int:
+    return group_rank if group is None else dist.get_global_rank(group, group_rank)
+
+
 def _all_gather_rows_async(local: torch.Tensor, plan: ZigZagPlan, group):
-    """Start the all-gather of ``_all_gather_rows``; the returned function
-    makes the current stream wait for it and returns the full tensor. Work
-    queued on the current stream in between overlaps the transfer."""
+    """Start gathering every rank's [B, 2*chunk, ...] rows into one
+    position-ordered [B, S, ...] tensor; the returned function makes the
+    current stream wait for the transfers and returns that tensor. Work
+    queued on the current stream in between overlaps the transfer.
+
+    One sequence (B == 1): the rows land in place, with no reorder copy. The
+    first chunks (rank r owns chunk r) arrive in rank order, which is position
+    order, by one all-gather into the first half; each rank's second chunk
+    (chunk 2W-1-r, i.e. the reverse of rank order) goes point to point
+    straight into its slot. Several sequences: one all-gather, then one
+    reorder copy."""
     W = plan.world
     B = local.shape[0]
+    c = plan.chunk
+    tail = tuple(local.shape[2:])
     src = local.contiguous()
-    flat = torch.empty((W * B,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
-    work = dist.all_gather_into_tensor(flat, src, group=group, async_op=True)
+    if B != 1:
+        flat = torch.empty((W * B,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        work = dist.all_gather_into_tensor(flat, src, group=group, async_op=True)
 
-    def finish(_src=src) -> torch.Tensor:  # _src: the collective reads it until done
-        work.wait()
-        return plan.unshard(list(flat.view((W, B) + tuple(local.shape[1:])).unbind(0)), dim=1)
+        def finish_batched(_src=src) -> torch.Tensor:  # _src: the collective reads it until done
+            work.wait()
+            return plan.unshard(list(flat.view((W, B) + tuple(local.shape[1:])).unbind(0)), dim=1)
+
+        return finish_batched
+    rank = dist.get_rank(group)
+    full = torch.empty((1, plan.seq_len) + tail, dtype=local.dtype, device=local.device)
+    rows = full.view((plan.seq_len,) + tail)
+    first, second = src[0, :c], src[0, c:]
+    works = [dist.all_gather_into_tensor(rows[: W * c], first, group=group, async_op=True)]
+    mine = 2 * W - 1 - rank
+    rows[mine * c:(mine + 1) * c].copy_(second)
+    ops = []
+    for p in range(W):
+        if p == rank:
+            continue
+        slot = 2 * W - 1 - p
+        ops.append(dist.P2POp(dist.isend, second, _group_peer(group, p), group))
+        ops.append(dist.P2POp(dist.irecv, rows[slot * c:(slot + 1) * c], _group_peer(group, p), group))
+    if ops:
+        works.extend(dist.batch_isend_irecv(ops))
+
+    def finish(_src=src) -> torch.Tensor:
+        for w in works:
+            w.wait()
+        return full
 
     return finish
 
@@ -129,6 +169,7 @@ class SequenceShardedBlock:
         self.rank = dist.get_rank(group)
         if dist.get_world_size(group) != plan.world:
             raise ValueError("plan.world does not match the process group size")
+        self._cache = {}
 
     # -- router over the gathered logits (hspmn_v2_1.py:95-122, eval) ------
     def _route(self, x_local: torch.Tensor, S: int) -> RouterOutput:
@@ -145,28 +186,50 @@ class SequenceShardedBlock:
         aux = r.sparsity_coef * sparsity_loss + r.entropy_coef * ent.mean()
         return RouterOutput(mask, indices, logits, aux)
 
-    def _local_selection(self, indices: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    def _chunk_tensors(self, device):
+        """(chunk bounds [4], local row positions [2*chunk]) on ``device``,
+        built once per device."""
+        key = str(device)
+        if key not in self._cache:
+            (s0, e0), (s1, e1) = self.plan.chunks(self.rank)
+            self._cache[key] = (torch.tensor([s0, e0, s1, e1], dtype=torch.int64, device=device),
+                                self.plan.local_positions(self.rank, device=device))
+        return self._cache[key]
+
+    def _selection_bounds_begin(self, indices: torch.Tensor):
+        """Where this rank's two chunks start and end in each sorted index row:
+        one searchsorted on the device, its [B,4] result copied to host memory
+        without waiting. ``_local_selection`` reads it once the independent
+        work of the forward is queued, so the host never drains the stream."""
+        bounds, _ = self._chunk_tensors(indices.device)
+        at = torch.searchsorted(indices, bounds.expand(indices.shape[0], 4).contiguous())
+        if not at.is_cuda:
+            return at, None
+        host = torch.empty(at.shape, dtype=at.dtype, pin_memory=True)
+        host.copy_(at, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return host, ev
+
+    def _local_selection(self, indices: torch.Tensor, pending) -> Tuple[torch.Tensor, torch.Tensor]:
         """Selected positions inside this rank's chunks (ascending, [B, K_r])
-        and their local row numbers. Requires B == 1 or equal counts per row."""
-        B = indices.shape[0]
-        pos_list, row_list = [], []
-        for b in range(B):
-            ib = indices[b]
-            ps, rs = [], []
-            off = 0
-            for s, e in self.plan.chunks(self.rank):
-                lo = int(torch.searchsorted(ib, torch.tensor(s, device=ib.device)))
-                hi = int(torch.searchsorted(ib, torch.tensor(e, device=ib.device)))
-                seg = ib[lo:hi]
-                ps.append(seg)
-                rs.append(seg - s + off)
-                off += e - s
-            pos_list.append(torch.cat(ps))
-            row_list.append(torch.cat(rs))
-        n = {p.numel() for p in pos_list}
-        if len(n) != 1:
+        and their local row numbers, from ``_selection_bounds_begin``'s
+        result. Requires B == 1 or equal counts per row."""
+        host, ev = pending
+        if ev is not None:
+            ev.synchronize()
+        at = host.tolist()
+        (s0, _), (s1, _) = self.plan.chunks(self.rank)
+        c = self.plan.chunk
+        counts = {(r[1] - r[0]) + (r[3] - r[2]) for r in at}
+        if len(counts) != 1:
             raise ValueError("per-sequence selection counts differ across the batch on this rank; "
                              "shard one sequence per call")
+        pos_list, row_list = [], []
+        for b, (lo0, hi0, lo1, hi1) in enumerate(at):
+            seg0, seg1 = indices[b, lo0:hi0], indices[b, lo1:hi1]
+            pos_list.append(torch.cat([seg0, seg1]))
+            row_list.append(torch.cat([seg0 - s0, seg1 - s1 + c]))
         return torch.stack(pos_list), torch.stack(row_list)
 
     def _halo_rows(self, h_local: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -226,10 +289,11 @@ class SequenceShardedBlock:
         if S_local != 2 * self.plan.chunk:
             raise ValueError(f"x_local has {S_local} rows; this rank owns {2 * self.plan.chunk}")
         ro = self._route(x_local, S)
+        pending = self._selection_bounds_begin(ro.indices)
         H, Hkv, hd = blk.num_heads, blk.num_kv_heads, blk.head_dim
         x_norm = blk.norm(x_local)
         cos, sin = blk.rope(x_local, S)
-        pos = self.plan.local_positions(self.rank, device=x_local.device).expand(B, S_local)
+        pos = self._chunk_tensors(x_local.device)[1].expand(B, S_local)
         # K (RoPE at the rows' global positions) and V of the local rows
         k_loc = self.ops.rope_gather_rows(blk.k_proj(x_norm).view(B, S_local, Hkv, hd), pos, cos, sin, False)
         v_loc = blk.v_proj(x_norm).view(B, S_local, Hkv, hd)
@@ -242,7 +306,7 @@ class SequenceShardedBlock:
         k_finish = _all_gather_rows_async(k_loc, self.plan, self.group)
         v_finish = _all_gather_rows_async(v_loc, self.plan, self.group)
         y = self._reflexive_end(x_local, h, before, after).contiguous()
-        sel_pos, sel_rows = self._local_selection(ro.indices)
+        sel_pos, sel_rows = self._local_selection(ro.indices, pending)
         if sel_pos.shape[1] > 0:
             # the routed queries of this rank: q_proj on those rows only, RoPE at
             # their global positions fused into the gather, o_proj on the K

@@ -52,7 +52,7 @@ enum hspmn_status {
 
 /* bits of the device-side flag word */
 #define HSPMN_DEVERR_POSITION 1u /* a query/selected position outside [0, S) */
-#define HSPMN_DEVERR_UNSORTED 2u /* scatter indices not strictly ascending */
+#define HSPMN_DEVERR_UNSORTED 2u /* indices not ascending where an entry point requires it (scatter, backward) */
 #define HSPMN_DEVERR_TIMEOUT 4u  /* a bounded pipeline wait in attention gave up */
 
 /* Library version, major*10000 + minor*100 + patch. */
@@ -146,6 +146,23 @@ HSPMN_API int hspmn_rope_gather_rows(const void* src, int64_t src_sb, int64_t sr
                                      int dtype, void* stream);
 
 /*
+ * Rotary embedding of every row of a [B,S,H,hd] tensor, row s at position
+ * pos0 + s: the K side of apply_rotary_pos_emb (hspmn_v2_1.py:66-68, applied
+ * at hspmn_v2_1.py:226-227) in one pass with no index array,
+ *   dst[b,s,h,:] = rope(src[b,s,h,:], pos0 + s)
+ * with rope() and its rounding as for hspmn_rope_gather_rows, so the rows are
+ * bit-identical to the reference's three tensor ops. Row strides in elements
+ * (src_sb, src_ss, dst_sb, dst_ss); each row's H*hd elements contiguous.
+ * cos/sin: tables of tab_rows rows (pos0 + S <= tab_rows), row stride tab_ss.
+ * dst may be src itself (same strides). hd a multiple of 16 (bf16/f16) or 8
+ * (f32); rows, strides and tables 16-byte aligned.
+ */
+HSPMN_API int hspmn_rope_rows(const void* src, int64_t src_sb, int64_t src_ss,
+                              const void* cos_tab, const void* sin_tab, int64_t tab_ss, int64_t tab_rows,
+                              int64_t pos0, void* dst, int64_t dst_sb, int64_t dst_ss,
+                              int64_t B, int64_t S, int64_t H, int64_t hd, int dtype, void* stream);
+
+/*
  * In-place residual add of the selected rows (hspmn_v2_1.py:238 where every
  * unselected row of o_proj(scatter(...)) is zero):
  *   dst[b, idx[b,i], :] = T(dst[b, idx[b,i], :] + src[b,i,:])
@@ -200,7 +217,9 @@ HSPMN_API int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int
  * a region where an allocation would synchronise the device or fail. The
  * split-KV partials go to a static buffer of
  * HSPMN_SQDK_NOALLOC_SCRATCH_BYTES (32 MiB) that is part of the library's
- * module on each device; the call itself allocates nothing.
+ * module on each device; the call itself allocates nothing. That buffer is
+ * device memory the library holds on every device its kernels are loaded on,
+ * from load until exit, whether or not this entry point is ever called.
  *
  * Arguments, results and error codes are those of hspmn_sqdk_fwd, plus
  * HSPMN_ERR_SCRATCH, returned without launching anything, for shapes whose
@@ -209,10 +228,12 @@ HSPMN_API int64_t hspmn_sqdk_workspace_size(int64_t B, int64_t K, int64_t S, int
  * rows can be).
  * Shapes with a workspace size of 0 do not touch the buffer.
  *
- * - The first call on each device (with that device current) looks up the
- *   buffer's device address and caches it; make that first call before any
- *   stream capture begins. The cached address is not refreshed after a
- *   cudaDeviceReset.
+ * - Validation runs in the same order as in hspmn_sqdk_fwd, with
+ *   HSPMN_ERR_SCRATCH where that function would find the workspace missing.
+ * - The first call on a device whose launch uses the buffer (with that device
+ *   current) looks up the buffer's device address and caches it; make such a
+ *   call before any stream capture begins. The cached address is not
+ *   refreshed after a cudaDeviceReset.
  * - Nothing in the buffer has to start at zero: every call writes each
  *   partial before it reads it.
  * - There is one buffer per device: calls on the same device whose work can
@@ -263,6 +284,10 @@ HSPMN_API int64_t hspmn_sqdk_bwd_workspace_size(int64_t B, int64_t K, int64_t H,
  * workspace: hspmn_sqdk_bwd_workspace_size() bytes (16-byte aligned; holds
  * rowsum(dO * O) and an fp32 dq accumulator). hd: multiple of 8, <= 128;
  * H / Hkv <= 64. With K == 0 the query-side pointers may be null.
+ * Each idx row must be ascending, as the router writes it: a key block finds
+ * its first query by binary search. (The forward takes any order.) A row
+ * found out of order sets HSPMN_DEVERR_UNSORTED; its gradients are then
+ * incomplete.
  */
 HSPMN_API int hspmn_sqdk_bwd(const void* q, const int64_t* q_strides,
                    const void* k, const int64_t* k_strides,

@@ -167,3 +167,29 @@ def test_block_bf16_cfg2_shape_against_oracle():
         y, _ = block(x)
         y_ref = block.reflexive(x) + block.o_proj(out.view(B, S, D))
     assert torch.equal(y, y_ref)
+
+
+@pytest.mark.gpu
+def test_fp32_block_attention_rounds_through_bf16():
+    """A float32 block's eval attention runs on the bf16 tensor-core kernel
+    (q, k, v rounded to bf16, fp32 accumulation, fp32 result), where the
+    reference's Triton path keeps tf32 dot products. Measured here against the
+    float32 oracle block (attention in fp32) on the same selection: the
+    difference stays inside the attention tolerance."""
+    seed_everything(5)
+    D, H, Hkv, S = 512, 8, 2, 1024
+    cfg = HSPMNConfig(dim=D, num_heads=H, num_kv_heads=Hkv, max_seq_len=S)
+    block = HSPMNBlock(cfg)
+    with torch.no_grad():
+        block.router.gate.weight.normal_(0, D ** -0.5)
+    params = {k: v.detach().float().numpy().copy() for k, v in block.state_dict().items()}
+    block = block.to(DEV).eval()
+    x = torch.randn(2, S, D, generator=torch.Generator().manual_seed(6))
+    with torch.no_grad():
+        out, _ = block(x.to(DEV))
+        idx = block.router(x.to(DEV)).indices.cpu().numpy()
+    ref, _, _, _ = oracle.block_forward(params, x.numpy(), H, Hkv, float(block.router.target_sparsity.item()),
+                                        cfg.rope_base, float(np.finfo(np.float32).eps), indices=idx)
+    err = np.abs(out.cpu().numpy() - ref)
+    print(f"fp32 block vs fp32 oracle: max_abs={err.max():.3e} mean_abs={err.mean():.3e}")
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())

@@ -65,6 +65,53 @@ def test_rope_gather_subnormal_and_huge(dtype, scale):
     assert bool(same.all())
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("B,S,H,hd,pos0", [(3, 701, 4, 128, 0), (2, 257, 16, 64, 100), (1, 33, 3, 16, 7),
+                                           (4, 1, 4, 128, 0)])
+def test_rope_rows_bit_exact(dtype, B, S, H, hd, pos0):
+    """RoPE over every row (position = pos0 + row), bit-identical to the
+    reference's three tensor ops on the same [B,H,S,hd] view; odd row counts
+    leave a lone last row for a warp."""
+    g = torch.Generator().manual_seed(B * S + hd)
+    rope = RotaryEmbedding(hd, 1024)
+    k = torch.randn(B, S, H, hd, generator=g).to(dtype)
+    cos, sin = rope(k, pos0 + S)
+    out = ops.rope_rows(k.to(DEV), cos.to(DEV), sin.to(DEV), pos0)
+    kt = k.to(DEV).transpose(1, 2)
+    c, s_ = cos[:, :, pos0:pos0 + S].to(DEV), sin[:, :, pos0:pos0 + S].to(DEV)
+    _, k_rot = apply_rotary_pos_emb(kt, kt, c, s_)
+    assert torch.equal(out, k_rot.transpose(1, 2))
+    # the numpy restatement of the per-op rounding agrees
+    ref = oracle.rope_rounded(k.float().numpy(), cos[0, 0, pos0:pos0 + S].float().numpy()[None, :, None, :],
+                              sin[0, 0, pos0:pos0 + S].float().numpy()[None, :, None, :], _NAME[dtype])
+    np.testing.assert_array_equal(out.float().cpu().numpy(), ref)
+
+
+def test_rope_rows_strided_and_in_place():
+    """A strided source (rows of a wider projection output) and dst == src
+    through the C ABI."""
+    import ctypes
+
+    from hspmn_b200 import _native as N
+    B, S, H, hd = 2, 300, 4, 128
+    g = torch.Generator().manual_seed(9)
+    rope = RotaryEmbedding(hd, 512)
+    wide = torch.randn(B, S, 2 * H * hd, generator=g).to(torch.bfloat16).to(DEV)
+    k = wide[:, :, :H * hd].view(B, S, H, hd)
+    cos, sin = rope(k, S)
+    cos2, sin2 = cos[0, 0].to(DEV).contiguous(), sin[0, 0].to(DEV).contiguous()
+    expect = ops.rope_rows(k.contiguous(), cos2, sin2, 0)
+    other = wide[:, :, H * hd:].clone()
+    rc = N.lib().hspmn_rope_rows(ctypes.c_void_p(k.data_ptr()), k.stride(0), k.stride(1),
+                                 ctypes.c_void_p(cos2.data_ptr()), ctypes.c_void_p(sin2.data_ptr()), hd, S, 0,
+                                 ctypes.c_void_p(k.data_ptr()), k.stride(0), k.stride(1), B, S, H, hd, N.HSPMN_BF16,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(k, expect)
+    assert torch.equal(wide[:, :, H * hd:], other)  # the rest of each row is left alone
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_scatter_add_rows_bit_exact(dtype):
     B, S, D, K = 3, 500, 256, 100

@@ -144,6 +144,23 @@ def test_rope_and_scatter_add_validation():
     assert rope(src=ctypes.c_void_p(4098)) == -3       # source not 16-byte aligned
     assert rope(B=0) == 0 and rope(K=0) == 0           # empty: nothing to do
 
+    def rows(**o):
+        a = dict(src=p, src_sb=8 * 2 * 128, src_ss=2 * 128, cos=p, sin=p, tab_ss=128, tab_rows=8, pos0=0,
+                 dst=p, dst_sb=8 * 2 * 128, dst_ss=2 * 128, B=1, S=8, H=2, hd=128, dt=bf16)
+        a.update(o)
+        return lib.hspmn_rope_rows(a["src"], a["src_sb"], a["src_ss"], a["cos"], a["sin"], a["tab_ss"],
+                                   a["tab_rows"], a["pos0"], a["dst"], a["dst_sb"], a["dst_ss"], a["B"], a["S"],
+                                   a["H"], a["hd"], a["dt"], None)
+
+    assert rows(cos=None) == -1                        # null pointer
+    assert rows(dt=bad) == -2
+    assert rows(pos0=1) == -1                          # positions past the table's last row
+    assert rows(pos0=-1) == -1
+    assert rows(tab_ss=64) == -1                       # table rows shorter than a head
+    assert rows(hd=12, tab_ss=12, src_ss=24, dst_ss=24, src_sb=192, dst_sb=192) == -4
+    assert rows(dst=ctypes.c_void_p(4104)) == -3       # destination not 16-byte aligned
+    assert rows(B=0) == 0 and rows(S=0, tab_rows=0) == 0
+
     def sadd(**o):
         a = dict(src=p, src_sb=4 * 2048, src_sk=2048, idx=p, idx_sb=4, dst=p, dst_sb=8 * 2048, dst_ss=2048,
                  B=1, S=8, K=4, row=2048, dt=bf16)

@@ -107,3 +107,43 @@ def test_tie_and_nan_order():
     # +0.0 ranks above -0.0 (bit order); both +0.0 ties kept in position order
     np.testing.assert_array_equal(idx[0], [0, 1, 2, 3, 5, 7])
     assert mask.sum() == 4
+
+
+@pytest.mark.parametrize("name", ["block_d64_H4_Hkv2_S128.npz", "block_d128_H4_Hkv1_S256.npz"])
+def test_torch_cpu_path_matches_reference(name):
+    """The torch restatement of the reference's CPU path (eager Flex), which
+    the bench times as the CPU baseline, reproduces the reference block's
+    outputs, selection and aux loss."""
+    import torch
+
+    from oracle.torch_cpu_ref import block_forward_torch
+
+    fx = G.load(name)
+    cfg = json.loads(fx["cfg"].item().decode())
+    shapes = G.block_shapes(cfg["dim"], cfg["num_heads"], cfg["num_kv_heads"])
+    cfg, x, params = G.block_inputs(fx, shapes)
+    sd = {k: torch.from_numpy(np.asarray(v, np.float32)) for k, v in params.items()}
+    sd["router.target_sparsity"] = torch.tensor(float(fx["target_sparsity"]), dtype=torch.float32)
+    out, aux, idx = block_forward_torch(sd, torch.from_numpy(x), cfg["num_heads"], cfg["num_kv_heads"],
+                                        cfg["rope_base"])
+    np.testing.assert_array_equal(idx.numpy(), fx["indices"])
+    np.testing.assert_allclose(out.numpy(), fx["out"], atol=1e-5, rtol=1e-5)
+    assert abs(float(aux) - float(fx["aux"])) <= 1e-6
+
+
+def test_torch_cpu_sqdk_pattern_matches_oracle():
+    """The reference's dense-masked PyTorch SQDK pattern (GQA by repeated K/V
+    heads) equals the numpy oracle."""
+    import torch
+
+    from oracle.torch_cpu_ref import sqdk_dense_torch
+
+    g = torch.Generator().manual_seed(3)
+    B, S, H, Hkv, hd, K = 2, 200, 6, 2, 32, 50
+    q = torch.randn(B, S, H, hd, generator=g)
+    k = torch.randn(B, S, Hkv, hd, generator=g)
+    v = torch.randn(B, S, Hkv, hd, generator=g)
+    idx = torch.stack([torch.sort(torch.randperm(S, generator=g)[:K])[0] for _ in range(B)])
+    out = sqdk_dense_torch(q, k, v, idx)
+    ref = oracle.sqdk_fp32(oracle.gather_rows(q.numpy(), idx.numpy()), k.numpy(), v.numpy(), idx.numpy())
+    np.testing.assert_allclose(out.numpy(), ref, atol=2e-5, rtol=1e-4)

@@ -96,7 +96,7 @@ def _sharded_worker(rank, world, port, out_path, dim, H, Hkv, S, sparsity):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("world", [1, 2, 4])
 def test_sequence_sharded_forward_matches_oracle(world):
     dim, H, Hkv, S, sparsity = 32, 4, 2, 64, 0.25
     with tempfile.TemporaryDirectory() as td:

@@ -71,6 +71,26 @@ def test_sqdk_bwd_f16():
         _close(name, got, ref)
 
 
+def test_unsorted_indices_flagged():
+    """The backward needs ascending index rows; a row out of order is
+    reported through the device flag word (the forward's output stays
+    correct: it takes any order). Sorted rows raise nothing."""
+    from hspmn_b200 import _native as N
+    q, k, v, d_o, idx = _inputs(1, 512, 8, 2, 128, 96, seed=21)
+    bad = idx.clone()
+    bad[0, 40], bad[0, 41] = idx[0, 41], idx[0, 40]
+    qd, kd, vd, dod, bd = (t.to(DEV) for t in (q, k, v, d_o, bad))
+    scale = 128 ** -0.5
+    ops.device_errors()  # clear
+    o, lse = ops.sqdk_fwd_lse(qd, kd, vd, bd, scale)
+    assert ops.device_errors() == 0
+    ref_o = oracle.sqdk_fp32(q.float().numpy(), k.float().numpy(), v.float().numpy(), bad.numpy())
+    assert np.abs(o.float().cpu().numpy() - ref_o).max() <= 2e-2
+    ops.sqdk_bwd(qd, kd, vd, bd, o, dod, lse, scale)
+    assert ops.device_errors() & N.DEVERR_UNSORTED
+    _run(q, k, v, d_o, idx)  # asserts a clean flag word for the sorted rows
+
+
 def test_fwd_lse_output_equals_fwd():
     q, k, v, _, idx = _inputs(2, 512, 16, 4, 128, 102, seed=4)
     qd, kd, vd, idd = (t.to(DEV) for t in (q, k, v, idx))

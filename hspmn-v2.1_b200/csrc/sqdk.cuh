@@ -31,10 +31,12 @@
 // Warp roles (192 threads, two CTAs per SM):
 //   warp 0      TMA producer: Q once, then K and V through 2-stage rings,
 //               K_{j+1} requested ahead of V_j
-//   warp 1      TMEM allocation + single-thread MMA issue: per block, Q K^T
-//               of block j, one commit, P V of block j-1 (the issuing
-//               thread's steps per block bound the pipeline, so it waits and
-//               commits as little as the ordering allows)
+//   warp 1      TMEM allocation + MMA issue: per block, Q K^T of block j,
+//               one commit, P V of block j-1. The warp runs the issue loop
+//               converged and one elected lane issues (operands stay
+//               warp-uniform, so each product costs its issuer far fewer
+//               cycles); it waits and commits as little as the ordering
+//               allows, since its steps per block bound the pipeline
 //   warps 2..5  softmax, lazy O correction, epilogue (row = TMEM lane): O / l
 //               staged in the freed Q tile, stored by one thread with TMA
 // Every mbarrier wait is bounded (common.cuh); a wait that gives up flags
@@ -280,7 +282,10 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0 && nblk > 0) {
+    // The warp runs the issue loop converged (operands stay warp-uniform,
+    // which makes each tcgen05.mma much cheaper to issue than from a lone
+    // lane); one elected lane issues every product and commit.
+    if (nblk > 0) {
       constexpr int kAB = kBF16 ? 1 : 0;
       constexpr uint32_t idesc_s = umma_idesc_f16(kSqdkBM, kSqdkBN, kAB, false, false);
       constexpr uint32_t idesc_o = umma_idesc_f16(kSqdkBM, HD, kAB, false, true);
@@ -293,31 +298,31 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
       // V block, MN-major: 16 keys = 2 groups of 8 rows (SBO 1024 B), hd in
       // 64-column chunks L::kKVChunkBytes apart (LBO)
       const uint64_t vdesc = sw128_desc(sbase + L::kVOff, L::kKVChunkBytes, 1024);
-      bool ok = mbar_wait(&bar_q, 0, &abort_flag);
+      bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_q, 0, &abort_flag));
       tc_fence_after();
       // P V of block jj once P_jj is written and V_jj has landed (one
       // overlapped probe of both barriers)
       auto issue_pv = [&](int jj) -> bool {
         const int s = jj % kSqdkStages, r = jj / kSqdkStages, sb = jj & 1;
-        if (!mbar_wait2(&bar_pfull[sb], (jj >> 1) & 1, &bar_vfull[s], r & 1, &abort_flag)) return false;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait2(&bar_pfull[sb], (jj >> 1) & 1, &bar_vfull[s], r & 1, &abort_flag)))
+          return false;
         tc_fence_after();
         const uint64_t vd = vdesc + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
         const uint32_t ta = tmem + sb * kSqdkBN;
-        umma_ts(tO, ta, vd, idesc_o, jj > 0 ? 1u : 0u);
+        umma_ts_warp(tO, ta, vd, idesc_o, jj > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 1; kk < kSqdkBN / 16; ++kk)
-          umma_ts(tO, ta + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_o, 1u);
-        if (!long_range) umma_commit(&bar_vempty[s]);
-        else if (jj == nblk - 2) umma_commit(&bar_vempty[0]);  // no Q K^T follows to signal it
+          umma_ts_warp(tO, ta + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_o, 1u);
+        if (!long_range) umma_commit_warp(&bar_vempty[s]);
+        else if (jj == nblk - 2) umma_commit_warp(&bar_vempty[0]);  // no Q K^T follows to signal it
         return true;
       };
       // unrolled by the ring depth: stage, buffer and descriptor offsets
-      // become constants (the issue thread's instruction count per block
-      // bounds the whole pipeline)
+      // become constants
 #pragma unroll 2
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kSqdkStages, r = j / kSqdkStages, sb = j & 1;
-        if (!mbar_wait(&bar_kfull[s], r & 1, &abort_flag)) {
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_kfull[s], r & 1, &abort_flag))) {
           ok = false;
           break;
         }
@@ -326,16 +331,17 @@ __global__ void __launch_bounds__(kSqdkThreads, 2)
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const int c = kk >> 2, w = kk & 3;  // 64-column chunk, 32-byte step inside the swizzle row
-          umma_ss(tmem + sb * kSqdkBN, qdesc + static_cast<uint64_t>((c * L::kQChunkBytes + w * 32) >> 4),
-                  kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
+          umma_ss_warp(tmem + sb * kSqdkBN, qdesc + static_cast<uint64_t>((c * L::kQChunkBytes + w * 32) >> 4),
+                       kd + static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bar_sfull[sb]);
+        umma_commit_warp(&bar_sfull[sb]);
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok) ok = issue_pv(nblk - 1);
-      if (ok) umma_commit(&bar_ofinal);
-      umma_commit(&bar_drain);
-      mbar_wait_drain(&bar_drain, 0);
+      if (ok) umma_commit_warp(&bar_ofinal);
+      umma_commit_warp(&bar_drain);
+      if (lane == 0) mbar_wait_drain(&bar_drain, 0);
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ softmax

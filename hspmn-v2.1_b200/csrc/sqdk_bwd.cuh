@@ -30,7 +30,8 @@
 // Warp roles (320 threads):
 //   warp 0      TMA producer: K and V once, Q_j and dO_j through a 2-stage
 //               ring; writes each block's per-row data (position, lse, Delta)
-//   warp 1      TMEM allocation + single-thread MMA issue
+//   warp 1      TMEM allocation + MMA issue (the converged warp runs the
+//               issue loop; one elected lane issues each product)
 //   warps 2..5  P^T / dS^T (thread = key), then the dK / dV epilogue
 //   warps 6..9  dQ: TMEM -> registers -> shared staging (thread = column d),
 //               then one thread issues the bulk reduces into global dQ
@@ -250,7 +251,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0 && nblk > 0) {
+    // The warp runs the issue loop converged (operands stay warp-uniform,
+    // which makes each tcgen05.mma much cheaper to issue than from a lone
+    // lane); one elected lane issues every product and commit.
+    if (nblk > 0) {
       constexpr int kAB = kBF16 ? 1 : 0;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBwdKeys, kBwdRows, kAB, false, false);
       constexpr uint32_t idesc_kv = umma_idesc_f16(kBwdKeys, kBwdHD, kAB, false, true);
@@ -265,43 +269,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // K read MN-major as the A of dQ^T (M = hd in 64-column chunks, K = keys)
       const uint64_t kdesc_mn = sw128_desc(sbase + L::kKOff, L::kKVChunkBytes, 1024);
       const uint64_t dsdesc = sw128_desc(sbase + L::kDSOff, L::kDSBytes, 1024);
-      bool ok = mbar_wait(&bar_kv, 0, &abort_flag);
+      bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_kv, 0, &abort_flag));
       tc_fence_after();
       auto issue_rest = [&](int jj) -> bool {
         const int set = jj & 1;
-        if (!mbar_wait(&bar_pfull[set], (jj >> 1) & 1, &abort_flag)) return false;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_pfull[set], (jj >> 1) & 1, &abort_flag))) return false;
         tc_fence_after();
         const uint32_t tS = tmem + set * L::kSetCols;
         const uint64_t rowoff = static_cast<uint64_t>((set * L::kRowBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBwdRows / 16; ++kk) {
           const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
-          umma_ts(tmem + L::kDVCol, tS + kk * 8, dodesc_mn + rowoff + step, idesc_kv, (jj > 0 || kk > 0) ? 1u : 0u);
+          umma_ts_warp(tmem + L::kDVCol, tS + kk * 8, dodesc_mn + rowoff + step, idesc_kv, (jj > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < kBwdRows / 16; ++kk) {
           const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
-          umma_ts(tmem + L::kDKCol, tS + 32 + kk * 8, qdesc_mn + rowoff + step, idesc_kv,
+          umma_ts_warp(tmem + L::kDKCol, tS + 32 + kk * 8, qdesc_mn + rowoff + step, idesc_kv,
                   (jj > 0 || kk > 0) ? 1u : 0u);
         }
         const uint64_t dsoff = static_cast<uint64_t>((set * L::kDSBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBwdKeys / 16; ++kk) {
           const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
-          umma_ss(tS + 64, kdesc_mn + step, dsdesc + dsoff + step, idesc_q, kk > 0 ? 1u : 0u);
+          umma_ss_warp(tS + 64, kdesc_mn + step, dsdesc + dsoff + step, idesc_q, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bar_dqfull[set]);
-        umma_commit(&bar_qempty[set]);
+        umma_commit_warp(&bar_dqfull[set]);
+        umma_commit_warp(&bar_qempty[set]);
         return true;
       };
       for (int j = 0; ok && j < nblk; ++j) {
         const int set = j & 1;
-        if (!mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag)) {
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag))) {
           ok = false;
           break;
         }
         // the dQ^T of block j-2 (in this set's dP^T columns) has been read
-        if (j >= 2 && !mbar_wait(&bar_setfree[set], ((j - 2) >> 1) & 1, &abort_flag)) {
+        if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bar_setfree[set], ((j - 2) >> 1) & 1, &abort_flag))) {
           ok = false;
           break;
         }
@@ -313,22 +317,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int c = kk >> 2, w = kk & 3;
           const uint64_t ka = static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4);
           const uint64_t qa = rowoff + static_cast<uint64_t>((c * L::kRowChunkBytes + w * 32) >> 4);
-          umma_ss(tS, kdesc + ka, qdesc + qa, idesc_s, kk > 0 ? 1u : 0u);
+          umma_ss_warp(tS, kdesc + ka, qdesc + qa, idesc_s, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < kBwdHD / 16; ++kk) {
           const int c = kk >> 2, w = kk & 3;
           const uint64_t va = static_cast<uint64_t>((c * L::kKVChunkBytes + w * 32) >> 4);
           const uint64_t da = rowoff + static_cast<uint64_t>((c * L::kRowChunkBytes + w * 32) >> 4);
-          umma_ss(tS + 64, vdesc + va, dodesc + da, idesc_s, kk > 0 ? 1u : 0u);
+          umma_ss_warp(tS + 64, vdesc + va, dodesc + da, idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bar_sfull[set]);
+        umma_commit_warp(&bar_sfull[set]);
         if (j >= 1 && !issue_rest(j - 1)) ok = false;
       }
       if (ok) ok = issue_rest(nblk - 1);
-      if (ok) umma_commit(&bar_final);
-      umma_commit(&bar_drain);
-      mbar_wait_drain(&bar_drain, 0);
+      if (ok) umma_commit_warp(&bar_final);
+      umma_commit_warp(&bar_drain);
+      if (lane == 0) mbar_wait_drain(&bar_drain, 0);
+      __syncwarp();
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ P^T, dS^T

@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--long-steps", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
-                    help="only the timed block steps (no parity, long-context, sweep, comparators)")
+                    help="only the timed steps (no parity, long-context, sweep or library comparators)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     a = ap.parse_args()
@@ -945,7 +945,8 @@ def headline_comparators(args, dev):
 def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
     rank, world, local_rank = dist_env()
     dev = init_dist(world, local_rank)
-    res = sqdk_sweep(args, dev, B, S, H, Hkv, fracs, comparators=fracs if len(fracs) == 1 else (0.05, 0.2))
+    comparators = () if args.no_extras else (fracs if len(fracs) == 1 else (0.05, 0.2))
+    res = sqdk_sweep(args, dev, B, S, H, Hkv, fracs, comparators=comparators)
     if rank == 0:
         for row in res["rows"]:
             print(json.dumps({"metric": "standalone SQDK: attention TFLOP/s and gather/scatter GB/s",

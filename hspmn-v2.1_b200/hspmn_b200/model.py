@@ -30,7 +30,7 @@ from . import ops
 from .utils import HSPMNConfig
 
 __all__ = ["HSPMNBlock", "TopKRouter", "HSPMNConfig", "RouterOutput", "RotaryEmbedding",
-           "apply_rotary_pos_emb", "rotate_half", "ReflexiveStream"]
+           "apply_rotary_pos_emb", "rotate_half", "ReflexiveStream", "depthwise_conv_seq"]
 
 
 class RouterOutput(NamedTuple):
@@ -165,9 +165,30 @@ class TopKRouter(nn.Module):
         return RouterOutput(mask, indices, logits, aux_loss)
 
 
+def depthwise_conv_seq(h: torch.Tensor, weight: torch.Tensor, padding: int = 1) -> torch.Tensor:
+    """``conv(h.transpose(1, 2)).transpose(1, 2)`` of ReflexiveStream.forward
+    (hspmn_v2_1.py:144) for ``h`` [B,S,D] and the depthwise Conv1d weight
+    [D,1,k]: the same convolution, computed as a 2-D depthwise convolution
+    of the [B,D,1,S] view of ``h``, whose memory is channels-last when ``h``
+    is contiguous. PyTorch then runs its channels-last depthwise kernel on
+    the memory as it lies and returns a contiguous [B,S,D] result, instead of
+    copying ``h`` into [B,D,S] order, running the generic depthwise kernel
+    and copying the transposed result again for the next GEMM. For bf16 and
+    fp32 the results are bit-identical to the reference's call; fp16 keeps
+    that call, since the channels-last kernel rounds a few fp16 outputs
+    differently (by one unit in the last place)."""
+    D = h.shape[2]
+    if h.dtype == torch.float16:
+        return F.conv1d(h.transpose(1, 2), weight, None, padding=padding, groups=D).transpose(1, 2)
+    y = F.conv2d(h.contiguous().permute(0, 2, 1).unsqueeze(2), weight.unsqueeze(2), None, padding=(0, padding),
+                 groups=D)
+    return y.squeeze(2).permute(0, 2, 1)
+
+
 class ReflexiveStream(nn.Module):
     """RMSNorm -> depthwise Conv1d(k=3) -> SwiGLU MLP, residual
-    (hspmn_v2_1.py:125-145). Stock PyTorch."""
+    (hspmn_v2_1.py:125-145). Stock PyTorch; the convolution is called in the
+    layout the [B,S,D] stream already has (``depthwise_conv_seq``)."""
 
     def __init__(self, dim: int, mlp_ratio: int = 4):
         super().__init__()
@@ -186,7 +207,7 @@ class ReflexiveStream(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         res = x
         x = self.norm(x)
-        x = self.conv(x.transpose(1, 2)).transpose(1, 2)
+        x = depthwise_conv_seq(x, self.conv.weight, self.conv.padding[0])
         return res + self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 

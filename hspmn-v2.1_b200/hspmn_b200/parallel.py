@@ -43,7 +43,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import ops as cuda_ops
-from .model import HSPMNBlock, RouterOutput
+from .model import HSPMNBlock, RouterOutput, depthwise_conv_seq
 
 
 def batch_slice(global_batch: int, rank: int, world: int) -> slice:
@@ -276,8 +276,7 @@ class SequenceShardedBlock:
         outs = []
         for i in range(2):
             seg = torch.cat([before[:, i:i + 1], h[:, i * c:(i + 1) * c], after[:, i:i + 1]], dim=1)
-            conv = F.conv1d(seg.transpose(1, 2), rf.conv.weight, None, padding=0, groups=rf.conv.groups)
-            outs.append(conv.transpose(1, 2))
+            outs.append(depthwise_conv_seq(seg, rf.conv.weight, padding=0))
         hc = torch.cat(outs, dim=1)
         return x_local + rf.down_proj(F.silu(rf.gate_proj(hc)) * rf.up_proj(hc))
 

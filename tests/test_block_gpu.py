@@ -193,3 +193,22 @@ def test_fp32_block_attention_rounds_through_bf16():
     err = np.abs(out.cpu().numpy() - ref)
     print(f"fp32 block vs fp32 oracle: max_abs={err.max():.3e} mean_abs={err.mean():.3e}")
     assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_reflexive_conv_layout_bit_exact(dtype):
+    """The reflexive stream's depthwise convolution, run channels-last on the
+    [B,S,D] memory, equals the reference's transposed Conv1d call bit for bit
+    on the GPU (hspmn_v2_1.py:144), at the block's width."""
+    from hspmn_b200.model import depthwise_conv_seq
+    g = torch.Generator(device=DEV).manual_seed(1)
+    D = 2048
+    conv = nn.Conv1d(D, D, 3, padding=1, groups=D, bias=False).to(DEV, dtype)
+    h = torch.randn(4, 1000, D, device=DEV, dtype=dtype, generator=g)
+    with torch.no_grad():
+        ref = conv(h.transpose(1, 2)).transpose(1, 2)
+        out = depthwise_conv_seq(h, conv.weight, 1)
+    if dtype != torch.float16:  # fp16 runs the reference's own call
+        assert out.is_contiguous()
+    assert torch.equal(out, ref)

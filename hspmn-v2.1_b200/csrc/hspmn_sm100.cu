@@ -721,6 +721,8 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
   prm.QTb = QTb;
   prm.hd = static_cast<int>(hd);
   prm.nkb = static_cast<int>((S + kBwdKeys - 1) / kBwdKeys);
+  // about one SM-count of CTAs per chunk of (sequence, head) pairs
+  prm.chunk = std::max(1, std::min(static_cast<int>(B * Hkv), sms / prm.nkb));
   prm.scale = sm_scale;
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
   const int64_t grid = static_cast<int64_t>(prm.nkb) * B * Hkv;
@@ -737,11 +739,11 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
       sqdk_bwd_dq_cast_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>(dq_acc, static_cast<__nv_bfloat16*>(dq), dqs[0],
                                                                   dqs[1], dqs[2], static_cast<int>(B),
                                                                   static_cast<int>(K), static_cast<int>(H),
-                                                                  static_cast<int>(hd));
+                                                                  static_cast<int>(hd), sm_scale);
     else
       sqdk_bwd_dq_cast_kernel<__half><<<g2, 256, 0, st>>>(dq_acc, static_cast<__half*>(dq), dqs[0], dqs[1], dqs[2],
                                                            static_cast<int>(B), static_cast<int>(K),
-                                                           static_cast<int>(H), static_cast<int>(hd));
+                                                           static_cast<int>(H), static_cast<int>(hd), sm_scale);
   }
   return launch_status();
 }

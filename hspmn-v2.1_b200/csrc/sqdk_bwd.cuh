@@ -11,30 +11,40 @@
 // reach n0 (indices are sorted: a suffix of the query list). Per block j:
 //   S^T  = K Q^T       tcgen05.mma SS, M=128 keys, N=64 rows, K=hd
 //   dP^T = V dO^T      tcgen05.mma SS, same shape
-//   P^T  = 2^(S^T c - lse2),  dS^T = scale P^T (dP^T - Delta)
+//   P^T  = 2^(S^T c - lse2),  dS^T / scale = P^T (dP^T - Delta)
 //                      one thread per key (TMEM lane); P^T and dS^T go back to
 //                      TMEM as 16-bit operands, dS^T also to shared memory
 //   dV  += P^T dO      tcgen05.mma TS (A = P^T in TMEM, B = dO MN-major)
 //   dK  += dS^T Q      tcgen05.mma TS (A = dS^T in TMEM, B = Q MN-major)
+//                      (dS^T / scale: dK and dQ take the scale in fp32, at the
+//                      dK store and in the dQ cast)
 //   dQ^T = K^T dS      tcgen05.mma SS (A = K MN-major, B = dS MN-major), into
-//                      the columns dP^T used; staged in shared memory and added
-//                      into an fp32 dQ in global memory with one bulk tensor
-//                      reduce per 64 columns (other key blocks add to the same
-//                      rows)
+//                      the columns dP^T used; staged in shared memory one
+//                      64-column chunk at a time and added into an fp32 dQ in
+//                      global memory with one bulk tensor reduce per chunk
+//                      (other key blocks add to the same rows)
 // dK and dV accumulate in TMEM over all query blocks and are stored once.
 //
 // TMEM (512 columns, one CTA per SM): two sets of [S^T | dP^T] (64 + 64
 // columns; block j uses set j % 2, so the next block's S^T and dP^T overlap
 // this block's softmax), dV (128), dK (128).
 //
-// Warp roles (320 threads):
-//   warp 0      TMA producer: K and V once, Q_j and dO_j through a 2-stage
-//               ring; writes each block's per-row data (position, lse, Delta)
+// Warp roles (448 threads):
+//   warp 0      TMA producer: K and V once, Q_j and dO_j through a 3-stage
+//               ring (a stage is refilled only after the dK / dV products of
+//               the block before last have read it, so two stages would leave
+//               the load latency exposed); writes each block's per-row data
+//               (position, lse, Delta) a block ahead into a 4-slot ring
 //   warp 1      TMEM allocation + MMA issue (the converged warp runs the
 //               issue loop; one elected lane issues each product)
-//   warps 2..5  P^T / dS^T (thread = key), then the dK / dV epilogue
+//   warps 2..5  P^T / dS^T of rows 0..31 (thread = key), then the dV store
 //   warps 6..9  dQ: TMEM -> registers -> shared staging (thread = column d),
 //               then one thread issues the bulk reduces into global dQ
+//   warps 10..13 P^T / dS^T of rows 32..63, then the dK store
+// Each softmax group writes its 16-bit P^T and dS^T only into the S^T
+// columns it read itself ([P^T 16 | dS^T 16] per 32 rows), so the two groups
+// need no ordering between them; the dV / dK products address each 16-row
+// step of their TMEM operand where its group put it.
 // Every mbarrier wait is bounded; a wait that gives up flags
 // HSPMN_DEVERR_TIMEOUT, the other roles stop, and the CTA drains its copies
 // and MMAs and frees its tensor memory before returning. TMEM loads and
@@ -49,9 +59,12 @@ namespace hspmn {
 
 constexpr int kBwdKeys = 128;   // keys per CTA (M of the key-major products)
 constexpr int kBwdRows = 64;    // rows (query, head) per query block
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 448;
+constexpr int kBwdSoftmaxArrivals = 8;  // softmax warps arriving on pfull per block
 constexpr int kBwdHD = 128;     // head_dim tile (hd <= 128; columns past hd are zero)
 constexpr int kBwdDQBar = 1;    // named barrier of the four dQ warps
+constexpr int kBwdStages = 3;   // Q / dO ring depth
+constexpr int kBwdInfo = 4;     // per-row block data ring depth (written one block ahead of the stage wait)
 static_assert(kBwdRows == 64, "the producer writes two rows of block data per lane");
 
 struct SqdkBwdLayout {
@@ -64,11 +77,11 @@ struct SqdkBwdLayout {
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kKVBytes;
   static constexpr int kQOff = kVOff + kKVBytes;
-  static constexpr int kDOOff = kQOff + 2 * kRowBytes;
-  static constexpr int kDSOff = kDOOff + 2 * kRowBytes;
+  static constexpr int kDOOff = kQOff + kBwdStages * kRowBytes;
+  static constexpr int kDSOff = kDOOff + kBwdStages * kRowBytes;
   static constexpr int kDQChunkBytes = kBwdRows * 64 * 4;  // 64 rows x 64 fp32 columns, row-major
   static constexpr int kDQOff = kDSOff + 2 * kDSBytes;
-  static constexpr int kBytes = kDQOff + kChunks * kDQChunkBytes;
+  static constexpr int kBytes = kDQOff + kDQChunkBytes;  // one 64-column chunk of dQ staged at a time
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kSetCols = 128;  // S^T at +0, dP^T / dQ^T at +64
@@ -87,15 +100,24 @@ struct SqdkBwdParams {
   void* dv;
   int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
   int B, K, S, H, Hkv, G, QTb, hd, nkb;
+  int chunk;  // (sequence, head) pairs per CTA-order chunk, >= 1
   float scale, scale_log2;
 };
 
-// Block index -> (key block kb, sequence b, kv head g); low key blocks (the
-// ones most queries see) first.
+// Block index -> (key block kb, sequence b, kv head g). The (sequence, head)
+// pairs are taken in chunks of p.chunk pairs, and inside a chunk the low key
+// blocks (the ones most queries see, the longest CTAs) come first. CTAs that
+// run at the same time then share a few pairs' Q, dO and dQ rows, which stay
+// in L2 across their key blocks; in key-block-major order every resident CTA
+// would stream a different pair's rows from HBM.
 __device__ __forceinline__ void sqdk_bwd_coords(const SqdkBwdParams& p, int item, int& kb, int& b, int& g) {
   const int BG = p.B * p.Hkv;
-  kb = item / BG;
-  const int bg = item - kb * BG;
+  const int per_chunk = p.chunk * p.nkb;
+  const int c = item / per_chunk;
+  const int r = item - c * per_chunk;
+  const int pairs = min(p.chunk, BG - c * p.chunk);
+  kb = r / pairs;
+  const int bg = c * p.chunk + (r - kb * pairs);
   b = bg / p.Hkv;
   g = bg - b * p.Hkv;
 }
@@ -107,12 +129,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const __grid_constant__ CUtensorMap tmDQ, const SqdkBwdParams p) {
   using L = SqdkBwdLayout;
   extern __shared__ uint8_t sqdk_bwd_smem_raw[];
-  __shared__ __align__(8) uint64_t bar_kv, bar_qfull[2], bar_qempty[2], bar_sfull[2], bar_pfull[2];
+  __shared__ __align__(8) uint64_t bar_kv, bar_qfull[kBwdStages], bar_qempty[kBwdStages], bar_sfull[2], bar_pfull[2];
   __shared__ __align__(8) uint64_t bar_dqfull[2], bar_setfree[2], bar_final, bar_drain;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int first_block_sh, nblk_sh;
-  __shared__ int info_pos[2][kBwdRows];
-  __shared__ float info_lse2[2][kBwdRows], info_delta[2][kBwdRows];
+  // per-row block data: position (-1 = no query), -lse in log2 units, -Delta
+  // (negated so the softmax adds them with packed f32x2 instructions), and
+  // whether every row of the block sees all 128 keys (no causal mask)
+  __shared__ __align__(16) int info_pos[kBwdInfo][kBwdRows];
+  __shared__ __align__(16) float info_nlse2[kBwdInfo][kBwdRows];
+  __shared__ __align__(16) float info_ndelta[kBwdInfo][kBwdRows];
+  __shared__ int info_full[kBwdInfo];
   __shared__ volatile uint32_t abort_flag;
 
   const uint32_t sbase = (smem_u32(sqdk_bwd_smem_raw) + 1023u) & ~1023u;
@@ -124,11 +151,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_kv, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kBwdStages; ++s) {
       mbar_init(&bar_qfull[s], 1);
       mbar_init(&bar_qempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_sfull[s], 1);
-      mbar_init(&bar_pfull[s], 4);
+      mbar_init(&bar_pfull[s], kBwdSoftmaxArrivals);
       mbar_init(&bar_dqfull[s], 1);
       mbar_init(&bar_setfree[s], 4);
     }
@@ -156,15 +185,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   {
     const int used = p.G * p.QTb;
     if (used < kBwdRows) {
-      for (int i = threadIdx.x; i < 2 * 2 * L::kChunks * (kBwdRows - used) * 8; i += kBwdThreads) {
+      for (int i = threadIdx.x; i < 2 * kBwdStages * L::kChunks * (kBwdRows - used) * 8; i += kBwdThreads) {
         const int unit = i & 7;
         int rest = i >> 3;
         const int row = used + rest % (kBwdRows - used);
         rest /= (kBwdRows - used);
         const int c = rest % L::kChunks;
         rest /= L::kChunks;
-        const int s = rest & 1;
-        const int which = rest >> 1;  // 0 = Q, 1 = dO
+        const int s = rest % kBwdStages;
+        const int which = rest / kBwdStages;  // 0 = Q, 1 = dO
         const uint32_t a =
             sbase + (which ? L::kDOOff : L::kQOff) + s * L::kRowBytes + c * L::kRowChunkBytes + row * 128 + unit * 16;
         st_shared_v4(a, make_uint4(0u, 0u, 0u, 0u));
@@ -189,48 +218,72 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_4d(sbase + L::kVOff + c * L::kKVChunkBytes, &tmV, &bar_kv, c * 64, g, n0, b);
       }
     }
-    for (int j = 0; j < nblk; ++j) {
-      const int s = j & 1;
-      const int qb = jb0 + j;
-      // this block's row data (two rows per lane), loaded before waiting for
-      // the stage: the loads do not touch it, so their latency overlaps the wait
-      int pos[2];
-      float lse2[2], dl[2];
+    // Row data of query block qb (two rows per lane): the raw position, the
+    // position before it, lse and Delta. Nothing here uses the loaded values:
+    // they are consumed (checked, converted, written to the ring) one
+    // iteration later, so the load latency never stalls the producer.
+    struct Rows {
+      int64_t ps[2], prev[2];
+      float lse[2], dl[2];
+      bool valid[2], first[2];
+    };
+    auto load_rows = [&](int qb, Rows& r) {
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int c = lane + 32 * u;
         const int qloc = c / p.G;
         const int qi = qb * p.QTb + qloc;
-        pos[u] = -1;
-        lse2[u] = 0.0f;
-        dl[u] = 0.0f;
-        if (qloc < p.QTb && qi < p.K) {
-          const int hh = g * p.G + (c - qloc * p.G);
-          const int64_t* ib = p.idx + static_cast<int64_t>(b) * p.idx_sb;
-          const int64_t ps = __ldg(ib + static_cast<int64_t>(qi) * p.idx_sk);
-          pos[u] = (ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
-          // the key block's first query came from a binary search over the
-          // row, which needs ascending positions; the key block at 0 visits
-          // every query block, so every row is checked by some CTA
-          if (hh == g * p.G && qi > 0 && ps < __ldg(ib + static_cast<int64_t>(qi - 1) * p.idx_sk))
-            raise_device_error(HSPMN_DEVERR_UNSORTED);
-          const int64_t ro = static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + hh;
-          lse2[u] = __ldg(p.lse + ro) * 1.4426950408889634f;
-          dl[u] = __ldg(p.delta + ro);
+        r.valid[u] = qloc < p.QTb && qi < p.K;
+        // the key block's first query came from a binary search over the
+        // row, which needs ascending positions; the key block at 0 visits
+        // every query block, so every row is checked by some CTA
+        r.first[u] = r.valid[u] && qi > 0 && c - qloc * p.G == 0;
+        r.ps[u] = -1;
+        r.prev[u] = -1;
+        r.lse[u] = 0.0f;
+        r.dl[u] = 0.0f;
+        if (r.valid[u]) {
+          const int64_t* ib = p.idx + static_cast<int64_t>(b) * p.idx_sb + static_cast<int64_t>(qi) * p.idx_sk;
+          r.ps[u] = __ldg(ib);
+          if (r.first[u]) r.prev[u] = __ldg(ib - p.idx_sk);
+          const int64_t ro =
+              static_cast<int64_t>(b) * p.row_sb + static_cast<int64_t>(qi) * p.row_sk + g * p.G + (c - qloc * p.G);
+          r.lse[u] = __ldg(p.lse + ro);
+          r.dl[u] = __ldg(p.delta + ro);
         }
       }
-      if (j >= 2) {
-        bool okw = true;
-        if (lane == 0) okw = mbar_wait(&bar_qempty[s], ((j - 2) >> 1) & 1, &abort_flag);
-        live = __shfl_sync(0xFFFFFFFFu, okw ? 1 : 0, 0) != 0;
-        if (!live) break;
-      }
+    };
+    // The row data of block j + 1 is loaded while block j waits for its
+    // stage, and written to the ring before block j + 1's wait: slot j % 4 was
+    // last read by the softmax of block j - 4, which finished before the dK /
+    // dV products of that block, whose completion freed the stage the
+    // producer waited for in iteration j - 1.
+    Rows rows;
+    if (nblk > 0) load_rows(jb0, rows);
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % kBwdStages;
+      const int slot = j & (kBwdInfo - 1);
+      const int qb = jb0 + j;
+      bool sees_all = true;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int c = lane + 32 * u;
-        info_pos[s][c] = pos[u];
-        info_lse2[s][c] = lse2[u];
-        info_delta[s][c] = dl[u];
+        const int64_t ps = rows.ps[u];
+        if (rows.first[u] && ps < rows.prev[u]) raise_device_error(HSPMN_DEVERR_UNSORTED);
+        const int pos = (!rows.valid[u] || ps < 0 || ps >= p.S) ? -1 : static_cast<int>(ps);
+        sees_all = sees_all && pos >= n0 + kBwdKeys - 1;
+        info_pos[slot][c] = pos;
+        info_nlse2[slot][c] = -(rows.lse[u] * 1.4426950408889634f);
+        info_ndelta[slot][c] = -rows.dl[u];
+      }
+      sees_all = __all_sync(0xFFFFFFFFu, sees_all);
+      if (lane == 0) info_full[slot] = sees_all ? 1 : 0;
+      if (j + 1 < nblk) load_rows(qb + 1, rows);
+      if (j >= kBwdStages) {
+        bool okw = true;
+        if (lane == 0) okw = mbar_wait(&bar_qempty[s], ((j - kBwdStages) / kBwdStages) & 1, &abort_flag);
+        live = __shfl_sync(0xFFFFFFFFu, okw ? 1 : 0, 0) != 0;
+        if (!live) break;
       }
       __syncwarp();
       if (lane == 0) {
@@ -246,8 +299,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (lane == 0 && nblk > 0) {
       mbar_wait_drain(&bar_kv, 0);
-      for (int s = 0; s < 2; ++s)
-        if (nq > s) mbar_wait_drain(&bar_qfull[s], ((nq - 1 - s) >> 1) & 1);
+      // the last load issued into each stage
+      for (int s = 0; s < kBwdStages; ++s) {
+        if (nq <= s) continue;
+        const int last = s + ((nq - 1 - s) / kBwdStages) * kBwdStages;
+        mbar_wait_drain(&bar_qfull[s], (last / kBwdStages) & 1);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
@@ -272,22 +329,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_kv, 0, &abort_flag));
       tc_fence_after();
       auto issue_rest = [&](int jj) -> bool {
-        const int set = jj & 1;
+        const int set = jj & 1, st = jj % kBwdStages;
         if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_pfull[set], (jj >> 1) & 1, &abort_flag))) return false;
         tc_fence_after();
         const uint32_t tS = tmem + set * L::kSetCols;
-        const uint64_t rowoff = static_cast<uint64_t>((set * L::kRowBytes) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
-          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
-          umma_ts_warp(tmem + L::kDVCol, tS + kk * 8, dodesc_mn + rowoff + step, idesc_kv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
-          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
-          umma_ts_warp(tmem + L::kDKCol, tS + 32 + kk * 8, qdesc_mn + rowoff + step, idesc_kv,
-                  (jj > 0 || kk > 0) ? 1u : 0u);
-        }
+        const uint64_t rowoff = static_cast<uint64_t>((st * L::kRowBytes) >> 4);
+        // dQ^T first, with its own commit: the dQ warps read it out of the
+        // dP^T columns while dV and dK run, so the next block but one can
+        // take those columns as soon as the pipe reaches it
         const uint64_t dsoff = static_cast<uint64_t>((set * L::kDSBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBwdKeys / 16; ++kk) {
@@ -295,23 +344,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_ss_warp(tS + 64, kdesc_mn + step, dsdesc + dsoff + step, idesc_q, kk > 0 ? 1u : 0u);
         }
         umma_commit_warp(&bar_dqfull[set]);
-        umma_commit_warp(&bar_qempty[set]);
+#pragma unroll
+        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
+          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
+          // rows 16 kk .. 16 kk + 15 of P^T: group kk / 2's columns [0, 16)
+          umma_ts_warp(tmem + L::kDVCol, tS + (kk >> 1) * 32 + (kk & 1) * 8, dodesc_mn + rowoff + step, idesc_kv,
+                       (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kBwdRows / 16; ++kk) {
+          const uint64_t step = static_cast<uint64_t>((kk * 16 * 128) >> 4);
+          // and of dS^T: group kk / 2's columns [16, 32)
+          umma_ts_warp(tmem + L::kDKCol, tS + (kk >> 1) * 32 + 16 + (kk & 1) * 8, qdesc_mn + rowoff + step, idesc_kv,
+                       (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit_warp(&bar_qempty[st]);
         return true;
       };
       for (int j = 0; ok && j < nblk; ++j) {
-        const int set = j & 1;
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag))) {
-          ok = false;
-          break;
-        }
-        // the dQ^T of block j-2 (in this set's dP^T columns) has been read
-        if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bar_setfree[set], ((j - 2) >> 1) & 1, &abort_flag))) {
+        const int set = j & 1, st = j % kBwdStages;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[st], (j / kBwdStages) & 1, &abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t tS = tmem + set * L::kSetCols;
-        const uint64_t rowoff = static_cast<uint64_t>((set * L::kRowBytes) >> 4);
+        const uint64_t rowoff = static_cast<uint64_t>((st * L::kRowBytes) >> 4);
+        // S^T into this set's first 64 columns, whose P^T / dS^T of block j-2
+        // the dV / dK products issued before it have read
 #pragma unroll
         for (int kk = 0; kk < kBwdHD / 16; ++kk) {
           const int c = kk >> 2, w = kk & 3;
@@ -319,6 +379,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t qa = rowoff + static_cast<uint64_t>((c * L::kRowChunkBytes + w * 32) >> 4);
           umma_ss_warp(tS, kdesc + ka, qdesc + qa, idesc_s, kk > 0 ? 1u : 0u);
         }
+        // dP^T goes where the dQ^T of block j-2 is: wait until it has been read
+        if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bar_setfree[set], ((j - 2) >> 1) & 1, &abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBwdHD / 16; ++kk) {
           const int c = kk >> 2, w = kk & 3;
@@ -335,73 +401,104 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (lane == 0) mbar_wait_drain(&bar_drain, 0);
       __syncwarp();
     }
-  } else if (warp < 6) {
+  } else if (warp < 6 || warp >= 10) {
     // ------------------------------------------------------------ P^T, dS^T
+    const int grp = warp >= 10 ? 1 : 0;    // rows 32 grp .. 32 grp + 31
     const int kr = 32 * (warp & 3) + lane;  // key row = TMEM lane
     const int n = n0 + kr;
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    const float c2 = p.scale_log2, sc = p.scale;
+    const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
     bool ok = nblk > 0;
+    // P^T and dS^T / scale of four rows c .. c + 3 from S^T and dP^T, two rows
+    // per packed f32x2 instruction; kMask applies the causal mask and drops
+    // rows without a query (blocks whose rows all see every key skip it). The
+    // softmax scale of dS is applied to dK and dQ in fp32 after the products.
+    auto rows4 = [&](auto kMaskTag, const uint32_t (&sv)[32], const uint32_t (&dv)[32], int o, int c, int slot,
+                     uint32_t& p01, uint32_t& p23, uint32_t& d01, uint32_t& d23) {
+      constexpr bool kMask = decltype(kMaskTag)::value;
+      const float4 nl = *reinterpret_cast<const float4*>(&info_nlse2[slot][c]);
+      const float4 nd = *reinterpret_cast<const float4*>(&info_ndelta[slot][c]);
+      float x0, x1, x2, x3;
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[o]), __uint_as_float(sv[o + 1])), c2, f2_pack(nl.x, nl.y)), x0, x1);
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[o + 2]), __uint_as_float(sv[o + 3])), c2, f2_pack(nl.z, nl.w)), x2,
+                x3);
+      float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2), e3 = fast_exp2(x3);
+      if constexpr (kMask) {
+        const int4 ps = *reinterpret_cast<const int4*>(&info_pos[slot][c]);
+        e0 = n <= ps.x ? e0 : 0.0f;
+        e1 = n <= ps.y ? e1 : 0.0f;
+        e2 = n <= ps.z ? e2 : 0.0f;
+        e3 = n <= ps.w ? e3 : 0.0f;
+      }
+      float g0, g1, g2, g3;
+      f2_unpack(f2_mul(f2_pack(e0, e1),
+                       f2_add(f2_pack(__uint_as_float(dv[o]), __uint_as_float(dv[o + 1])), f2_pack(nd.x, nd.y))),
+                g0, g1);
+      f2_unpack(f2_mul(f2_pack(e2, e3),
+                       f2_add(f2_pack(__uint_as_float(dv[o + 2]), __uint_as_float(dv[o + 3])), f2_pack(nd.z, nd.w))),
+                g2, g3);
+      p01 = pack2<kBF16>(e0, e1);
+      p23 = pack2<kBF16>(e2, e3);
+      d01 = pack2<kBF16>(g0, g1);
+      d23 = pack2<kBF16>(g2, g3);
+    };
     for (int j = 0; ok && j < nblk; ++j) {
-      const int set = j & 1;
+      const int set = j & 1, slot = j & (kBwdInfo - 1);
       // the row data of this block (written by the producer before its
       // arrival) and the S^T / dP^T of this block
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[set], (j >> 1) & 1, &abort_flag) &&
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_qfull[j % kBwdStages], (j / kBwdStages) & 1, &abort_flag) &&
                                        mbar_wait(&bar_sfull[set], (j >> 1) & 1, &abort_flag));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + set * L::kSetCols;
-      uint32_t sr[2][32], dr[2][32];
-      tmem_ld32(tS, sr[0]);
-      tmem_ld32(tS + 32, sr[1]);
-      tmem_ld32(tS + 64, dr[0]);
-      tmem_ld32(tS + 96, dr[1]);
-      tmem_wait_ld();
-      uint32_t pp[32], dd[32];
+      uint32_t pp[16], dd[16];
+      {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tS + 32 * grp, sr);
+        tmem_ld32(tS + 64 + 32 * grp, dr);
+        tmem_wait_ld();
+        if (info_full[slot]) {
 #pragma unroll
-      for (int c = 0; c < kBwdRows; c += 2) {
-        float pv[2], dv[2];
+          for (int o = 0; o < 32; o += 4)
+            rows4(std::false_type{}, sr, dr, o, 32 * grp + o, slot, pp[o >> 1], pp[(o >> 1) + 1], dd[o >> 1],
+                  dd[(o >> 1) + 1]);
+        } else {
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int cc = c + u;
-          const float s = __uint_as_float(sr[cc >> 5][cc & 31]);
-          const float dp = __uint_as_float(dr[cc >> 5][cc & 31]);
-          const float pr = (n <= info_pos[set][cc]) ? fast_exp2(s * c2 - info_lse2[set][cc]) : 0.0f;
-          pv[u] = pr;
-          dv[u] = sc * pr * (dp - info_delta[set][cc]);
+          for (int o = 0; o < 32; o += 4)
+            rows4(std::true_type{}, sr, dr, o, 32 * grp + o, slot, pp[o >> 1], pp[(o >> 1) + 1], dd[o >> 1],
+                  dd[(o >> 1) + 1]);
         }
-        pp[c >> 1] = pack2<kBF16>(pv[0], pv[1]);
-        dd[c >> 1] = pack2<kBF16>(dv[0], dv[1]);
       }
-      tmem_st32(tS, pp);
-      tmem_st32(tS + 32, dd);
-      // dS^T row of this key into the MN-major B tile of dQ^T: 128 bytes,
-      // 16-byte units XOR-swizzled by key % 8
+      // [P^T | dS^T] of the group's 32 rows into the S^T columns it read
+      tmem_st16(tS + 32 * grp, pp);
+      tmem_st16(tS + 32 * grp + 16, dd);
+      // the group's half of this key's dS^T row in the MN-major B tile of
+      // dQ^T: 128 bytes per key, 16-byte units XOR-swizzled by key % 8
       const uint32_t rowb = sbase + L::kDSOff + set * L::kDSBytes + kr * 128;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        st_shared_v4(rowb + ((u ^ (kr & 7)) << 4), make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]));
+      for (int u = 0; u < 4; ++u)
+        st_shared_v4(rowb + (((4 * grp + u) ^ (kr & 7)) << 4),
+                     make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]));
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_pfull[set]);
     }
-    // ------------------------------------------------------------ dK / dV
+    // ------------------------------------------------------------ dV (group 0) / dK (group 1)
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_final, 0, &abort_flag));
     using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
     // the TMEM loads are warp-collective: every lane runs them, only the
     // stores depend on the lane's key being inside the sequence
     if (ok || nblk == 0) {
       tc_fence_after();
-      Elt* dvrow = static_cast<Elt*>(p.dv) + static_cast<int64_t>(b) * p.dv_sb + static_cast<int64_t>(n) * p.dv_ss +
-                   static_cast<int64_t>(g) * p.dv_sh;
-      Elt* dkrow = static_cast<Elt*>(p.dk) + static_cast<int64_t>(b) * p.dk_sb + static_cast<int64_t>(n) * p.dk_ss +
-                   static_cast<int64_t>(g) * p.dk_sh;
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        Elt* row = which ? dkrow : dvrow;
-        const uint32_t tcol = tmem + lane_base + (which ? L::kDKCol : L::kDVCol);
+      Elt* row = grp ? static_cast<Elt*>(p.dk) + static_cast<int64_t>(b) * p.dk_sb + static_cast<int64_t>(n) * p.dk_ss +
+                           static_cast<int64_t>(g) * p.dk_sh
+                     : static_cast<Elt*>(p.dv) + static_cast<int64_t>(b) * p.dv_sb + static_cast<int64_t>(n) * p.dv_ss +
+                           static_cast<int64_t>(g) * p.dv_sh;
+      const uint32_t tcol = tmem + lane_base + (grp ? L::kDKCol : L::kDVCol);
+      const float f = grp ? p.scale : 1.0f;
+      {
 #pragma unroll 1
         for (int c = 0; c < kBwdHD; c += 32) {
           uint32_t rr[32];
@@ -417,10 +514,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const int col = c + 8 * v;
             if (n < p.S && col < p.hd) {
               uint4 w;
-              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]), __uint_as_float(rr[8 * v + 1]));
-              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]), __uint_as_float(rr[8 * v + 3]));
-              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]), __uint_as_float(rr[8 * v + 5]));
-              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]), __uint_as_float(rr[8 * v + 7]));
+              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * f, __uint_as_float(rr[8 * v + 1]) * f);
+              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * f, __uint_as_float(rr[8 * v + 3]) * f);
+              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * f, __uint_as_float(rr[8 * v + 5]) * f);
+              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * f, __uint_as_float(rr[8 * v + 7]) * f);
               *reinterpret_cast<uint4*>(row + col) = w;
             }
           }
@@ -447,25 +544,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_setfree[set]);
-      // the previous block's reduces have read the staging tile
-      if (warp == 6 && lane == 0) tma_store_wait_read();
-      named_bar_sync(kBwdDQBar, 128);
-      // dQ^T column d of the 64 rows -> row-major staging, one 64-column chunk
-      // per TMA box (a warp writes 32 consecutive floats of a row at a time)
-      const uint32_t col = sbase + L::kDQOff + (d >> 6) * L::kDQChunkBytes + (d & 63) * 4;
+      // one 64-column chunk at a time through the staging tile: the two warps
+      // holding the chunk's columns write it (a warp writes 32 consecutive
+      // floats of a row at a time), one thread issues its bulk reduce
+      const uint32_t col = sbase + L::kDQOff + (d & 63) * 4;
+      for (int ch = 0; ch < L::kChunks && ch * 64 < p.hd; ++ch) {
+        // the previous reduce has read the staging tile
+        if (warp == 6 && lane == 0) tma_store_wait_read();
+        named_bar_sync(kBwdDQBar, 128);
+        if ((d >> 6) == ch) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + c * 256), "r"(r0[c]) : "memory");
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + (c + 32) * 256), "r"(r1[c]) : "memory");
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(kBwdDQBar, 128);
-      if (warp == 6 && lane == 0) {
-        // rows past the K selected queries are clipped by the tensor map
-        const int qb = jb0 + j;
-        for (int ch = 0; ch < L::kChunks && ch * 64 < p.hd; ++ch)
-          tma_reduce_add_4d(&tmDQ, sbase + L::kDQOff + ch * L::kDQChunkBytes, ch * 64, g * p.G, qb * p.QTb, b);
-        tma_store_commit();
+          for (int c = 0; c < 32; ++c) {
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + c * 256), "r"(r0[c]) : "memory");
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(col + (c + 32) * 256), "r"(r1[c]) : "memory");
+          }
+          fence_proxy_async_smem();
+        }
+        named_bar_sync(kBwdDQBar, 128);
+        if (warp == 6 && lane == 0) {
+          // rows past the K selected queries are clipped by the tensor map
+          tma_reduce_add_4d(&tmDQ, sbase + L::kDQOff, ch * 64, g * p.G, (jb0 + j) * p.QTb, b);
+          tma_store_commit();
+        }
       }
     }
     if (warp == 6 && lane == 0) tma_store_wait_read();
@@ -502,11 +602,12 @@ __global__ void __launch_bounds__(256) sqdk_bwd_delta_kernel(const T* __restrict
   }
 }
 
-// dq (fp32 accumulator, dense [B,K,H,hd]) -> the caller's dtype and strides.
+// scale x dq (fp32 accumulator of K^T (dS / scale), dense [B,K,H,hd]) -> the
+// caller's dtype and strides.
 template <typename T>
 __global__ void __launch_bounds__(256) sqdk_bwd_dq_cast_kernel(const float* __restrict__ acc, T* __restrict__ dq,
                                                               int64_t sb, int64_t sk, int64_t sh, int B, int K, int H,
-                                                              int hd) {
+                                                              int hd, float scale) {
   const int64_t n = static_cast<int64_t>(B) * K * H * hd;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; e < n;
        e += static_cast<int64_t>(gridDim.x) * 256) {
@@ -517,7 +618,7 @@ __global__ void __launch_bounds__(256) sqdk_bwd_dq_cast_kernel(const float* __re
     rest /= H;
     const int64_t i = rest % K;
     const int64_t b = rest / K;
-    dq[b * sb + i * sk + h * sh + d] = static_cast<T>(acc[e]);
+    dq[b * sb + i * sk + h * sh + d] = static_cast<T>(acc[e] * scale);
   }
 }
 

@@ -30,7 +30,8 @@
 // this block's softmax), dV (128), dK (128).
 //
 // Warp roles (448 threads):
-//   warp 0      TMA producer: K and V once, Q_j and dO_j through a 3-stage
+//   warp 0      setup: K / V loads, then the search for the first query
+//               block; TMA producer: Q_j and dO_j through a 3-stage
 //               ring (a stage is refilled only after the dK / dV products of
 //               the block before last have read it, so two stages would leave
 //               the load latency exposed); writes each block's per-row data
@@ -165,16 +166,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&bar_drain, 1);
     abort_flag = 0u;
     fence_mbar_init();
-    // first query whose position reaches n0 (positions ascend along the row)
+    // K and V of the key block do not depend on the query range: their loads
+    // start before the search below (drained before exit even if no query
+    // block turns out to see these keys)
+    mbar_arrive_expect_tx(&bar_kv, 2 * L::kKVBytes);
+    for (int c = 0; c < L::kChunks; ++c) {
+      tma_load_4d(sbase + L::kKOff + c * L::kKVChunkBytes, &tmK, &bar_kv, c * 64, g, n0, b);
+      tma_load_4d(sbase + L::kVOff + c * L::kKVChunkBytes, &tmV, &bar_kv, c * 64, g, n0, b);
+    }
+  }
+  if (warp == 0) {
+    // First query whose position reaches n0 (positions ascend along the row):
+    // a 32-way search, each round one load per lane over an interval 32 times
+    // shorter than the last (two rounds for a thousand queries instead of ten
+    // dependent loads). The answer stays in [lo, hi].
     const int64_t* ib = p.idx + static_cast<int64_t>(b) * p.idx_sb;
     int lo = 0, hi = p.K;
     while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (__ldg(ib + static_cast<int64_t>(mid) * p.idx_sk) < n0) lo = mid + 1;
-      else hi = mid;
+      const int step = (hi - lo + 31) / 32;
+      const int at = lo + lane * step;
+      const bool below = at < hi && __ldg(ib + static_cast<int64_t>(at) * p.idx_sk) < n0;
+      const int c = __popc(__ballot_sync(0xFFFFFFFFu, below));
+      if (c == 0) break;  // idx[lo] >= n0
+      const int nlo = lo + (c - 1) * step + 1;
+      hi = min(hi, lo + c * step);
+      lo = nlo;
     }
-    first_block_sh = lo / p.QTb;
-    nblk_sh = lo < p.K ? nqb - lo / p.QTb : 0;
+    if (lane == 0) {
+      first_block_sh = lo / p.QTb;
+      nblk_sh = lo < p.K ? nqb - lo / p.QTb : 0;
+    }
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, L::kTmemCols);
@@ -211,13 +232,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ------------------------------------------------------------ producer
     int nq = 0;
     bool live = true;
-    if (lane == 0 && nblk > 0) {
-      mbar_arrive_expect_tx(&bar_kv, 2 * L::kKVBytes);
-      for (int c = 0; c < L::kChunks; ++c) {
-        tma_load_4d(sbase + L::kKOff + c * L::kKVChunkBytes, &tmK, &bar_kv, c * 64, g, n0, b);
-        tma_load_4d(sbase + L::kVOff + c * L::kKVChunkBytes, &tmV, &bar_kv, c * 64, g, n0, b);
-      }
-    }
     // Row data of query block qb (two rows per lane): the raw position, the
     // position before it, lse and Delta. Nothing here uses the loaded values:
     // they are consumed (checked, converted, written to the ring) one
@@ -297,7 +311,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       ++nq;
     }
-    if (lane == 0 && nblk > 0) {
+    if (lane == 0) {
       mbar_wait_drain(&bar_kv, 0);
       // the last load issued into each stage
       for (int s = 0; s < kBwdStages; ++s) {

@@ -658,7 +658,7 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
   }
   const CUtensorMapDataType dt =
       dtype == HSPMN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdk, mdv;
   std::memset(&mq, 0, sizeof(mq));
   std::memset(&mdo, 0, sizeof(mdo));
   if (K > 0) {
@@ -682,6 +682,13 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
                             static_cast<uint64_t>(vs[0] * es)};
     if (int rc = encode_4d(&mk, k, dt, dims, sk, box)) return rc;
     if (int rc = encode_4d(&mv, v, dt, dims, sv, box)) return rc;
+    // dV / dK leave the kernel through TMA stores of the same 64 x 128-key tile
+    const uint64_t sdk[3] = {static_cast<uint64_t>(dks[2] * es), static_cast<uint64_t>(dks[1] * es),
+                             static_cast<uint64_t>(dks[0] * es)};
+    const uint64_t sdv[3] = {static_cast<uint64_t>(dvs[2] * es), static_cast<uint64_t>(dvs[1] * es),
+                             static_cast<uint64_t>(dvs[0] * es)};
+    if (int rc = encode_4d(&mdk, dk, dt, dims, sdk, box)) return rc;
+    if (int rc = encode_4d(&mdv, dv, dt, dims, sdv, box)) return rc;
   }
   // the fp32 dq accumulator, added into per query block with bulk tensor reduces
   CUtensorMap mdq;
@@ -730,7 +737,8 @@ int hspmn_sqdk_bwd(const void* q, const int64_t* qs, const void* k, const int64_
   auto kern = dtype == HSPMN_BF16 ? sqdk_bwd_kernel<true> : sqdk_bwd_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SqdkBwdLayout::kAlloc) != cudaSuccess)
     return HSPMN_ERR_CUDA;
-  kern<<<static_cast<unsigned>(grid), kBwdThreads, SqdkBwdLayout::kAlloc, st>>>(mq, mk, mv, mdo, mdq, prm);
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, SqdkBwdLayout::kAlloc, st>>>(mq, mk, mv, mdo, mdq, mdv, mdk,
+                                                                                 prm);
   if (int rc = launch_status()) return rc;
   if (K > 0) {
     const int64_t n = B * K * H * hd;

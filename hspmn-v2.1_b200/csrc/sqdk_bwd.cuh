@@ -64,6 +64,7 @@ constexpr int kBwdThreads = 448;
 constexpr int kBwdSoftmaxArrivals = 8;  // softmax warps arriving on pfull per block
 constexpr int kBwdHD = 128;     // head_dim tile (hd <= 128; columns past hd are zero)
 constexpr int kBwdDQBar = 1;    // named barrier of the four dQ warps
+constexpr int kBwdEpiBar = 2;   // named barriers 2 and 3: the dV / dK store of each softmax group
 constexpr int kBwdStages = 3;   // Q / dO ring depth
 constexpr int kBwdInfo = 4;     // per-row block data ring depth (written one block ahead of the stage wait)
 static_assert(kBwdRows == 64, "the producer writes two rows of block data per lane");
@@ -127,7 +128,8 @@ template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     sqdk_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const __grid_constant__ CUtensorMap tmDQ, const SqdkBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDV,
+                    const __grid_constant__ CUtensorMap tmDK, const SqdkBwdParams p) {
   using L = SqdkBwdLayout;
   extern __shared__ uint8_t sqdk_bwd_smem_raw[];
   __shared__ __align__(8) uint64_t bar_kv, bar_qfull[kBwdStages], bar_qempty[kBwdStages], bar_sfull[2], bar_pfull[2];
@@ -501,41 +503,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     // ------------------------------------------------------------ dV (group 0) / dK (group 1)
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bar_final, 0, &abort_flag));
-    using Elt = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-    // the TMEM loads are warp-collective: every lane runs them, only the
-    // stores depend on the lane's key being inside the sequence
+    // The group's 128 x 128 accumulator goes through shared memory (the Q
+    // ring, idle once every product has completed) in the 128-byte-swizzled
+    // layout of the K / V tiles, one 16 KB tile per 64 columns, and out with
+    // one TMA store per tile (keys past S and columns past hd are clipped by
+    // the tensor map). Storing each key's row straight from registers would
+    // write 16-byte pieces of 128 rows 1 KB apart. The TMEM loads are
+    // warp-collective: every lane runs them.
     if (ok || nblk == 0) {
       tc_fence_after();
-      Elt* row = grp ? static_cast<Elt*>(p.dk) + static_cast<int64_t>(b) * p.dk_sb + static_cast<int64_t>(n) * p.dk_ss +
-                           static_cast<int64_t>(g) * p.dk_sh
-                     : static_cast<Elt*>(p.dv) + static_cast<int64_t>(b) * p.dv_sb + static_cast<int64_t>(n) * p.dv_ss +
-                           static_cast<int64_t>(g) * p.dv_sh;
       const uint32_t tcol = tmem + lane_base + (grp ? L::kDKCol : L::kDVCol);
       const float f = grp ? p.scale : 1.0f;
-      {
+      const uint32_t stg = sbase + L::kQOff + grp * L::kKVBytes;
 #pragma unroll 1
-        for (int c = 0; c < kBwdHD; c += 32) {
-          uint32_t rr[32];
-          if (nblk > 0) {
-            tmem_ld32(tcol + c, rr);
-            tmem_wait_ld();
-          } else {
+      for (int c = 0; c < kBwdHD; c += 32) {
+        uint32_t rr[32];
+        if (nblk > 0) {
+          tmem_ld32(tcol + c, rr);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) rr[i] = 0u;
-          }
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int col = c + 8 * v;
-            if (n < p.S && col < p.hd) {
-              uint4 w;
-              w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * f, __uint_as_float(rr[8 * v + 1]) * f);
-              w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * f, __uint_as_float(rr[8 * v + 3]) * f);
-              w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * f, __uint_as_float(rr[8 * v + 5]) * f);
-              w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * f, __uint_as_float(rr[8 * v + 7]) * f);
-              *reinterpret_cast<uint4*>(row + col) = w;
-            }
-          }
+          for (int i = 0; i < 32; ++i) rr[i] = 0u;
         }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int col = c + 8 * v;
+          uint4 w;
+          w.x = pack2<kBF16>(__uint_as_float(rr[8 * v + 0]) * f, __uint_as_float(rr[8 * v + 1]) * f);
+          w.y = pack2<kBF16>(__uint_as_float(rr[8 * v + 2]) * f, __uint_as_float(rr[8 * v + 3]) * f);
+          w.z = pack2<kBF16>(__uint_as_float(rr[8 * v + 4]) * f, __uint_as_float(rr[8 * v + 5]) * f);
+          w.w = pack2<kBF16>(__uint_as_float(rr[8 * v + 6]) * f, __uint_as_float(rr[8 * v + 7]) * f);
+          const int unit = (col & 63) >> 3;
+          st_shared_v4(stg + (col >> 6) * L::kKVChunkBytes + kr * 128 + ((unit ^ (kr & 7)) << 4), w);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(kBwdEpiBar + grp, 128);
+      if ((warp & 3) == 2 && lane == 0) {
+        for (int ch = 0; ch < L::kChunks && ch * 64 < p.hd; ++ch)
+          tma_store_4d(grp ? &tmDK : &tmDV, stg + ch * L::kKVChunkBytes, ch * 64, g, n0, b);
+        tma_store_commit();
+        tma_store_wait_read();
       }
     }
   } else {

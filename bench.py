@@ -156,7 +156,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, smax, reasons, n = [], [], set(), 0
+        sm, smax, pw, reasons, n = [], [], [], set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
             for line in f:
@@ -168,13 +168,17 @@ class ClockSampler:
                     smax.append(float(parts[2]))
                 except ValueError:
                     continue
+                try:
+                    pw.append(float(parts[3]))
+                except ValueError:
+                    pass
                 n += 1
                 for name, val in zip(names, parts[5:9]):
                     if val.lower().startswith("active"):
                         reasons.add(name)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": n}
+                "power_w": statistics.median(pw) if pw else None, "reasons": sorted(reasons), "samples": n}
 
 
 # ---------------------------------------------------------------------------
@@ -1006,6 +1010,17 @@ def run_sqdk_bwd(args):
             ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
         e1.record()
         torch.cuda.synchronize()
+        # clocks and power under the same launches, over about a second (the
+        # timed steps alone are shorter than nvidia-smi's sampling period)
+        clocks = ClockSampler([local_rank]) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        barrier(world)
+        reps = max(1, int(1500.0 / max(e0.elapsed_time(e1) / args.steps, 0.05)))
+        for _ in range(reps):
+            ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
+        torch.cuda.synchronize()
+        clock_info = clocks.stop() if clocks else None
         assert ops.device_errors(dev) == 0
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
     if rank == 0:
@@ -1019,7 +1034,9 @@ def run_sqdk_bwd(args):
                                                                f"k={args.sparsity} (K={K}) per GPU"},
             "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak, "unit": "TFLOP/s",
                          "frac": tf / world / peak, "peak_source": f"{peak_src} bf16 dense, burst",
-                         "flops_per_launch": flops}}), flush=True)
+                         "frac_of_sustained_peak": tf / world / float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])),
+                         "flops_per_launch": flops},
+            "clocks": clock_info}), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -429,18 +429,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // per packed f32x2 instruction; kMask applies the causal mask and drops
     // rows without a query (blocks whose rows all see every key skip it). The
     // softmax scale of dS is applied to dK and dQ in fp32 after the products.
+    // Each lane holds the row data of row 32 grp + lane and the rows reach
+    // the other lanes by shuffles: a broadcast 16-byte shared load costs four
+    // shared-memory wavefronts, and shared-memory bandwidth is what bounds
+    // this kernel (tensor-core operand reads, TMA, staging).
+    float my_nl = 0.0f, my_nd = 0.0f;
     auto rows4 = [&](auto kMaskTag, const uint32_t (&sv)[32], const uint32_t (&dv)[32], int o, int c, int slot,
                      uint32_t& p01, uint32_t& p23, uint32_t& d01, uint32_t& d23) {
       constexpr bool kMask = decltype(kMaskTag)::value;
-      const float4 nl = *reinterpret_cast<const float4*>(&info_nlse2[slot][c]);
-      const float4 nd = *reinterpret_cast<const float4*>(&info_ndelta[slot][c]);
+      const float4 nl = make_float4(__shfl_sync(0xFFFFFFFFu, my_nl, o), __shfl_sync(0xFFFFFFFFu, my_nl, o + 1),
+                                    __shfl_sync(0xFFFFFFFFu, my_nl, o + 2), __shfl_sync(0xFFFFFFFFu, my_nl, o + 3));
+      const float4 nd = make_float4(__shfl_sync(0xFFFFFFFFu, my_nd, o), __shfl_sync(0xFFFFFFFFu, my_nd, o + 1),
+                                    __shfl_sync(0xFFFFFFFFu, my_nd, o + 2), __shfl_sync(0xFFFFFFFFu, my_nd, o + 3));
       float x0, x1, x2, x3;
       f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[o]), __uint_as_float(sv[o + 1])), c2, f2_pack(nl.x, nl.y)), x0, x1);
       f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[o + 2]), __uint_as_float(sv[o + 3])), c2, f2_pack(nl.z, nl.w)), x2,
                 x3);
       float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2), e3 = fast_exp2(x3);
       if constexpr (kMask) {
-        const int4 ps = *reinterpret_cast<const int4*>(&info_pos[slot][c]);
+        const int my_ps = info_pos[slot][c - o + lane];
+        const int4 ps = make_int4(__shfl_sync(0xFFFFFFFFu, my_ps, o), __shfl_sync(0xFFFFFFFFu, my_ps, o + 1),
+                                  __shfl_sync(0xFFFFFFFFu, my_ps, o + 2), __shfl_sync(0xFFFFFFFFu, my_ps, o + 3));
         e0 = n <= ps.x ? e0 : 0.0f;
         e1 = n <= ps.y ? e1 : 0.0f;
         e2 = n <= ps.z ? e2 : 0.0f;
@@ -473,6 +482,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld32(tS + 32 * grp, sr);
         tmem_ld32(tS + 64 + 32 * grp, dr);
         tmem_wait_ld();
+        my_nl = info_nlse2[slot][32 * grp + lane];
+        my_nd = info_ndelta[slot][32 * grp + lane];
         if (info_full[slot]) {
 #pragma unroll
           for (int o = 0; o < 32; o += 4)

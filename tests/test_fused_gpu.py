@@ -20,7 +20,7 @@ def _sorted_idx(B, S, K, g):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("H,hd", [(16, 128), (4, 64), (4, 16)])
+@pytest.mark.parametrize("H,hd", [(16, 128), (4, 64), (4, 16), (5, 48)])  # hd=48: column groups that do not divide 32
 @pytest.mark.parametrize("by_position", [True, False])
 def test_rope_gather_bit_exact(dtype, H, hd, by_position):
     B, S, K = 2, 700, 140
@@ -67,7 +67,7 @@ def test_rope_gather_subnormal_and_huge(dtype, scale):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("B,S,H,hd,pos0", [(3, 701, 4, 128, 0), (2, 257, 16, 64, 100), (1, 33, 3, 16, 7),
-                                           (4, 1, 4, 128, 0)])
+                                           (4, 1, 4, 128, 0), (2, 65, 5, 48, 3)])
 def test_rope_rows_bit_exact(dtype, B, S, H, hd, pos0):
     """RoPE over every row (position = pos0 + row), bit-identical to the
     reference's three tensor ops on the same [B,H,S,hd] view; odd row counts

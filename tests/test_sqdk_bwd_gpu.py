@@ -50,7 +50,10 @@ def _run(q, k, v, d_o, idx):
 
 @pytest.mark.parametrize("B,S,H,Hkv,hd,K", [
     (1, 256, 4, 2, 64, 40), (2, 300, 8, 2, 128, 60), (1, 512, 16, 4, 128, 102), (1, 200, 6, 2, 64, 50),
-    (1, 130, 2, 2, 128, 33), (2, 1024, 16, 4, 128, 205), (1, 96, 4, 4, 48, 96), (1, 640, 8, 1, 96, 17)])
+    (1, 130, 2, 2, 128, 33), (2, 1024, 16, 4, 128, 205), (1, 96, 4, 4, 48, 96), (1, 640, 8, 1, 96, 17),
+    # CTA order in chunks of (sequence, head) pairs: 9 pairs at 32 key blocks are chunks of
+    # 4, 4 and 1; 157 key blocks give chunks of one pair
+    (3, 4096, 6, 3, 64, 100), (1, 20000, 2, 2, 64, 30)])
 def test_sqdk_bwd_against_oracle(B, S, H, Hkv, hd, K):
     q, k, v, d_o, idx = _inputs(B, S, H, Hkv, hd, K, seed=S + K)
     o, lse, dq, dk, dv = _run(q, k, v, d_o, idx)

@@ -66,6 +66,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Adds `bytes` to the current phase's expected transaction count without an
+// arrival (the phase still needs its arrivals).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
 // One probe of the phase with this parity. try_wait without a suspend-time
 // hint: the waiting thread is parked for the hardware's own short interval
 // and rechecks. (A 200 us hint measured 4-5 % slower on the attention

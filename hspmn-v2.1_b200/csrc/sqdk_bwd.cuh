@@ -197,6 +197,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       first_block_sh = lo / p.QTb;
       nblk_sh = lo < p.K ? nqb - lo / p.QTb : 0;
+      // the first query block's Q / dO are requested now (bytes expected, no
+      // arrival): the producer arrives once the block's row data is written,
+      // so the stage cannot complete before the softmax may read that data
+      if (lo < p.K) {
+        mbar_expect_tx(&bar_qfull[0], static_cast<uint32_t>(2 * L::kChunks * p.G * p.QTb * 128));
+        for (int c = 0; c < L::kChunks; ++c) {
+          tma_load_4d(sbase + L::kQOff + c * L::kRowChunkBytes, &tmQ, &bar_qfull[0], c * 64, g * p.G,
+                      (lo / p.QTb) * p.QTb, b);
+          tma_load_4d(sbase + L::kDOOff + c * L::kRowChunkBytes, &tmDO, &bar_qfull[0], c * 64, g * p.G,
+                      (lo / p.QTb) * p.QTb, b);
+        }
+      }
     }
   }
   if (warp == 1) {
@@ -302,7 +314,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!live) break;
       }
       __syncwarp();
-      if (lane == 0) {
+      if (lane == 0 && j == 0) {
+        mbar_arrive(&bar_qfull[0]);  // its loads were issued at setup
+      } else if (lane == 0) {
         mbar_arrive_expect_tx(&bar_qfull[s], static_cast<uint32_t>(2 * L::kChunks * p.G * p.QTb * 128));
         for (int c = 0; c < L::kChunks; ++c) {
           tma_load_4d(sbase + L::kQOff + s * L::kRowBytes + c * L::kRowChunkBytes, &tmQ, &bar_qfull[s], c * 64,

@@ -833,6 +833,9 @@ def run_block(args):
                 # comparators at the headline attention shape (B=64, K=820, S=4096, GQA 4)
                 extras["gpu_comparator_headline"] = headline_comparators(args, dev)
                 free_cuda()
+                # the training path's SQDK backward at the same attention shape
+                extras["sqdk_bwd"] = sqdk_bwd_measure(args, dev, rank, world, local_rank, 10, 3)
+                free_cuda()
 
     if world > 1:
         import torch.distributed as dist
@@ -974,19 +977,18 @@ def run_sweep(args, B=8, S=32768, H=16, Hkv=16, fracs=(0.05, 0.1, 0.2, 0.5)):
         dist.destroy_process_group()
 
 
-def run_sqdk_bwd(args):
+def sqdk_bwd_measure(args, dev, rank, world, local_rank, steps, warmup):
     """Backward of the SQDK attention at the block's attention shape
     (--batch/--seq-len/--heads/--kv-heads/--sparsity, hd = dim / heads): the
     selected rows of a random sorted selection, the forward with log-sum-exp
     once, then timed launches of the backward (rowsum(dO*O), the key-block
     kernel, the dq cast). Algorithmic FLOPs: 10 * hd per (row, visible key)
-    (S^T, dP^T, dV, dK, dQ), i.e. 2.5 x the forward's."""
+    (S^T, dP^T, dV, dK, dQ), i.e. 2.5 x the forward's. Returns rank 0's
+    figures (max over ranks) and the clocks seen under the same launches."""
     import torch
 
     from hspmn_b200 import ops
 
-    rank, world, local_rank = dist_env()
-    dev = init_dist(world, local_rank)
     B, S, H, Hkv = args.batch, args.seq_len, args.heads, args.kv_heads
     hd = args.dim // H
     K = max(1, int(S * args.sparsity))
@@ -1001,12 +1003,12 @@ def run_sqdk_bwd(args):
     with torch.no_grad():
         o, lse = ops.sqdk_fwd_lse(q, k, v, idx, scale)
         flops = 10.0 * hd * H * float((idx + 1).sum().item())
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
         e1.record()
         torch.cuda.synchronize()
@@ -1016,27 +1018,40 @@ def run_sqdk_bwd(args):
         if clocks:
             clocks.start()
         barrier(world)
-        reps = max(1, int(1500.0 / max(e0.elapsed_time(e1) / args.steps, 0.05)))
+        reps = max(1, int(1500.0 / max(e0.elapsed_time(e1) / steps, 0.05)))
         for _ in range(reps):
             ops.sqdk_bwd(q, k, v, idx, o, d_o, lse, scale)
         torch.cuda.synchronize()
         clock_info = clocks.stop() if clocks else None
         assert ops.device_errors(dev) == 0
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    tf = flops / (ms / 1e3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    return {"workload": f"SQDK backward B={B} S={S} H={H} Hkv={Hkv} hd={hd} k={args.sparsity} (K={K}) per GPU",
+            "ms_per_launch": ms, "TFLOP_s": tf, "frac_of_burst_peak": tf / peak,
+            "frac_of_sustained_peak": tf / float(peaks.get("bf16_tflops_sustained",
+                                                            FALLBACK_PEAKS["bf16_tflops_sustained"])),
+            "peak": peak, "peak_source": f"{peak_src} bf16 dense, burst", "flops_per_launch": flops,
+            "launches_timed": steps, "clocks": clock_info}
+
+
+def run_sqdk_bwd(args):
+    """The SQDK backward alone (see sqdk_bwd_measure), one JSON line."""
+    rank, world, local_rank = dist_env()
+    dev = init_dist(world, local_rank)
+    res = sqdk_bwd_measure(args, dev, rank, world, local_rank, args.steps, args.warmup)
     if rank == 0:
-        tf = flops * world / (ms / 1e3) / 1e12
-        peak = float(peaks["bf16_tflops"])
+        tf = res["TFLOP_s"] * world
         print(json.dumps({
             "metric": "SQDK backward: attention-gradient TFLOP/s", "value": tf, "unit": "TFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_launch"],
             "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic: N(0,1) q/k/v/dO, "
-            "random sorted selection", "config": {"workload": f"SQDK backward B={B} S={S} H={H} Hkv={Hkv} hd={hd} "
-                                                               f"k={args.sparsity} (K={K}) per GPU"},
-            "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak, "unit": "TFLOP/s",
-                         "frac": tf / world / peak, "peak_source": f"{peak_src} bf16 dense, burst",
-                         "frac_of_sustained_peak": tf / world / float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])),
-                         "flops_per_launch": flops},
-            "clocks": clock_info}), flush=True)
+            "random sorted selection", "config": {"workload": res["workload"]},
+            "roofline": {"bound": "tensor", "achieved": res["TFLOP_s"], "peak": res["peak"], "unit": "TFLOP/s",
+                         "frac": res["frac_of_burst_peak"], "peak_source": res["peak_source"],
+                         "frac_of_sustained_peak": res["frac_of_sustained_peak"],
+                         "flops_per_launch": res["flops_per_launch"]},
+            "clocks": res["clocks"]}), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

